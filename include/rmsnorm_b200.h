@@ -1,0 +1,164 @@
+/*
+ * rmsnorm_b200.h -- C ABI of the B200 (sm_100a) RMSNorm forward/backward library.
+ *
+ * This is the whole native boundary of the package: plain pointers, sizes and
+ * status codes. No C++ exception crosses it, no torch type appears in it, and
+ * the library never allocates device memory on a call: the caller owns every
+ * buffer (inputs, outputs, backward workspace) and the stream.
+ *
+ * Interfaces of the reference (Int21-AI/RMSNorm-H100) that it replaces:
+ *   rmsnorm_b200_fwd        <- rmsnorm_cuda_fwd (rmsnorm/csrc/ptx_rmsnorm_kernels.cu:7296-7321)
+ *                              reached through the pybind entry points fwd_, fwd_fast and
+ *                              fwd_residual_fast (rmsnorm/csrc/torch_bindings.cpp:120-194, 268-310)
+ *   rmsnorm_b200_bwd        <- rmsnorm_cuda_bwd (ptx_rmsnorm_kernels.cu:7323-7351) reached
+ *                              through bwd_ and bwd_fast (torch_bindings.cpp:196-266, 312-352)
+ *   rmsnorm_b200_bwd_workspace_size
+ *                           <- rmsnorm_cuda_bwd_partial_blocks / rmsnorm_cuda_bwd_reduce_chunks
+ *                              (ptx_rmsnorm_kernels.cu:7275-7281), which the bindings used to
+ *                              size dw_partial (torch_bindings.cpp:241-254, 317-340)
+ *   rmsnorm_b200_strerror   <- the TORCH_CHECK / CUDA_CHECK messages that the reference threw
+ *                              across its extern "C" boundary (ptx_rmsnorm_kernels.cu:42-50,
+ *                              7232-7234; torch_bindings.cpp:50-70)
+ *   rmsnorm_b200_device_status, rmsnorm_b200_set_wait_timeout_ns,
+ *   rmsnorm_b200_selftest_wait_timeout
+ *                           <- no counterpart: the reference's mbarrier waits are unbounded
+ *                              (ptx_rmsnorm_kernels.cu:957-986). Every wait here is bounded
+ *                              and reports through a device status word.
+ *   rmsnorm_b200_abi_version, rmsnorm_b200_launch_count, rmsnorm_b200_last_plan
+ *                           <- no counterpart (introspection for tests and benchmarks).
+ *
+ * Semantics (identical to the reference's fp32 math, rmsnorm/rmsnorm.py:230-271, 390-399):
+ *   rows are the flattened leading dimensions; row r uses affine head (r % heads).
+ *   fwd:  h = x (+ residual) in fp32; rstd = rsqrt(mean(h^2) + eps);
+ *         out = h * rstd * weight (+ bias); residual_out = h; rstd[r] = rstd.
+ *   bwd:  xhat = x * rstd; wdy = dout * weight;  c = mean(xhat * wdy);
+ *         dx = (wdy - xhat * c) * rstd (+ dresidual_out); dresidual = dx;
+ *         dweight = sum_rows(dout * xhat); dbias = sum_rows(dout), reduced in a fixed
+ *         order (bitwise reproducible run to run on the same device model).
+ */
+#ifndef RMSNORM_B200_H_
+#define RMSNORM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RMSNORM_B200_ABI_VERSION 1
+
+/* dtype codes: same numbering as the reference's dtype_code() (torch_bindings.cpp:37-48). */
+enum {
+  RMSNORM_B200_F16 = 0,
+  RMSNORM_B200_BF16 = 1,
+  RMSNORM_B200_F32 = 2
+};
+
+/* status codes */
+enum {
+  RMSNORM_B200_OK = 0,
+  RMSNORM_B200_ERR_INVALID_ARGUMENT = 1,
+  RMSNORM_B200_ERR_UNSUPPORTED = 2,
+  RMSNORM_B200_ERR_WORKSPACE = 3,
+  RMSNORM_B200_ERR_CUDA = 4,
+  RMSNORM_B200_ERR_DEVICE_TIMEOUT = 5,
+  RMSNORM_B200_ERR_NO_DEVICE = 6
+};
+
+/* Forward arguments. Pointers marked nullable may be NULL. All row-major, contiguous. */
+typedef struct rmsnorm_b200_fwd_args {
+  int64_t rows;               /* M >= 0 (rows after flattening; tokens*heads when per-head) */
+  int64_t hidden;             /* N >= 1 */
+  int32_t heads;              /* H >= 1; rows % H == 0; row r uses affine head r % H */
+  int32_t x_dtype;
+  const void* x;              /* [rows, hidden] */
+  const void* residual;       /* nullable, [rows, hidden] */
+  int32_t residual_dtype;
+  int32_t weight_dtype;
+  const void* weight;         /* nullable, [weight_heads, hidden] */
+  int32_t weight_heads;       /* 1 (shared) or heads (per-head) */
+  int32_t bias_dtype;
+  const void* bias;           /* nullable, [bias_heads, hidden] */
+  int32_t bias_heads;         /* 1 or heads */
+  int32_t out_dtype;
+  void* out;                  /* [rows, hidden] */
+  void* residual_out;         /* nullable, [rows, hidden]; receives x (+ residual) */
+  int32_t residual_out_dtype;
+  int32_t reserved0;
+  float* rstd;                /* nullable, [rows] fp32 */
+  float eps;
+  int32_t reserved1;
+} rmsnorm_b200_fwd_args;
+
+/* Backward arguments. */
+typedef struct rmsnorm_b200_bwd_args {
+  int64_t rows;
+  int64_t hidden;
+  int32_t heads;
+  int32_t x_dtype;
+  const void* x;              /* [rows, hidden]: the normalised input (x or residual_out) */
+  const void* dout;           /* [rows, hidden] */
+  int32_t dout_dtype;
+  int32_t weight_dtype;
+  const float* rstd;          /* [rows] fp32 */
+  const void* weight;         /* nullable, [weight_heads, hidden] */
+  int32_t weight_heads;
+  int32_t dresidual_out_dtype;
+  const void* dresidual_out;  /* nullable, [rows, hidden]; added to dx */
+  void* dx;                   /* [rows, hidden] */
+  int32_t dx_dtype;
+  int32_t dresidual_dtype;
+  void* dresidual;            /* nullable, [rows, hidden]; a second copy of dx */
+  void* dweight;              /* nullable (requires weight), [weight_heads, hidden] */
+  int32_t dweight_dtype;
+  int32_t dbias_dtype;
+  void* dbias;                /* nullable, [dbias_heads, hidden]: sum of dout over rows */
+  int32_t dbias_heads;        /* 1 or heads */
+  int32_t reserved0;
+} rmsnorm_b200_bwd_args;
+
+/* Enqueue the forward on `stream` (a cudaStream_t; NULL = legacy default stream).
+ * Uses the current CUDA device. Returns a status code; never blocks the host. */
+int rmsnorm_b200_fwd(const rmsnorm_b200_fwd_args* args, void* stream);
+
+/* Bytes of device workspace rmsnorm_b200_bwd needs for these arguments on the current
+ * device (0 when no dweight/dbias is requested). The size depends on the device's SM count. */
+int rmsnorm_b200_bwd_workspace_size(const rmsnorm_b200_bwd_args* args, size_t* bytes);
+
+/* Enqueue the backward on `stream`. `workspace` must be device memory of at least
+ * rmsnorm_b200_bwd_workspace_size() bytes, 16-byte aligned; its contents on entry are
+ * ignored and it may be reused as soon as the stream has passed this call. */
+int rmsnorm_b200_bwd(const rmsnorm_b200_bwd_args* args, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* Static, human-readable message for a status code. */
+const char* rmsnorm_b200_strerror(int status);
+
+/* Reads (and optionally clears) the current device's status word, in stream order:
+ * 0 when no kernel has reported a problem, RMSNORM_B200_ERR_DEVICE_TIMEOUT when a bounded
+ * device-side wait ran out. Synchronises `stream`. */
+int rmsnorm_b200_device_status(void* stream, int32_t* status, int32_t* where, int32_t clear);
+
+/* Upper bound of every device-side wait on the current device (default 2 s). */
+int rmsnorm_b200_set_wait_timeout_ns(uint64_t timeout_ns);
+
+/* Failure-detection self test: launches one CTA that waits, with the given bound, on an
+ * mbarrier nothing ever arrives at. The wait runs out, the kernel records
+ * RMSNORM_B200_ERR_DEVICE_TIMEOUT in the status word and returns; nothing faults. */
+int rmsnorm_b200_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
+
+int rmsnorm_b200_abi_version(void);
+
+/* Number of kernels this library has launched in this process (all devices). */
+uint64_t rmsnorm_b200_launch_count(void);
+
+/* Describes the plan of the last fwd/bwd call on this host thread (kernel family,
+ * cluster size, grid, stage layout). Returns the full length; writes at most len-1 chars. */
+int rmsnorm_b200_last_plan(char* buf, size_t len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RMSNORM_B200_H_ */

@@ -1,0 +1,180 @@
+# SPDX-License-Identifier: MIT
+"""ORACLE -- test infrastructure only. Not part of the product.
+
+CPU restatement of the reference's fp32 RMSNorm math (Int21-AI/RMSNorm-H100), used as the
+checker by tests/, by `__graft_entry__.smoke()` and by `bench.py`'s CPU-baseline /
+reference arm. The product (`rmsnorm` package + librmsnorm_b200.so) never imports it.
+
+Parity is pinned: tests/test_oracle_golden.py checks these functions against golden
+vectors produced by the reference package itself (tests/golden/make_golden.py imports the
+reference and runs its CPU path), and against the C restatement in oracle/rmsnorm_ref.c.
+
+Every function names the reference lines it restates (paths inside the reference repo).
+All math is fp32 on the host, in the reference's operation order.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+
+def sum_to_affine_shape(values: Tensor, affine_shape) -> Tensor:
+    """rmsnorm/rmsnorm.py:196-204: sum the leading dims so the result has the affine shape."""
+    extra = values.dim() - len(affine_shape)
+    return values if extra == 0 else values.sum(dim=tuple(range(extra)))
+
+
+def fwd(
+    x: Tensor,
+    weight: Optional[Tensor] = None,
+    bias: Optional[Tensor] = None,
+    residual: Optional[Tensor] = None,
+    eps: float = 1e-6,
+    out_dtype: Optional[torch.dtype] = None,
+    residual_dtype: Optional[torch.dtype] = None,
+):
+    """rmsnorm/rmsnorm.py:246-271 (`_fallback_fwd`; equal to `rmsnorm_ref` :230-243 for its
+    outputs). Returns (out, residual_out, rstd, y_f32): out in out_dtype (default x.dtype),
+    residual_out = x + residual rounded to residual_dtype (default residual.dtype; None when
+    there is no residual), rstd with shape x.shape[:-1], and the unrounded fp32 output."""
+    out_dtype = out_dtype or x.dtype
+    h = x.cpu().float()
+    if residual is not None:
+        h = h + residual.cpu().float()
+    rstd = torch.rsqrt(torch.mean(h.square(), dim=-1, keepdim=True) + eps)
+    y = h * rstd
+    if weight is not None:
+        y = y * weight.cpu().float()
+    if bias is not None:
+        y = y + bias.cpu().float()
+    ro = None
+    if residual is not None:
+        ro = h.to(residual_dtype or residual.dtype)
+    elif residual_dtype is not None and residual_dtype != x.dtype:
+        ro = x.cpu().to(residual_dtype)
+    return y.to(out_dtype), ro, rstd.squeeze(-1), y
+
+
+def bwd(
+    x: Tensor,
+    weight: Optional[Tensor],
+    dout: Tensor,
+    rstd: Tensor,
+    dresidual_out: Optional[Tensor] = None,
+    has_bias: bool = False,
+    bias_shape=None,
+):
+    """rmsnorm/rmsnorm.py:390-399 (`rmsnorm_bwd_ref`) plus the dresidual_out and dbias terms
+    of :452-464. Returns fp32 (dx, dweight, dbias, sum_abs_dw, sum_abs_db):
+      dx = (wdy - xhat * mean(xhat * wdy)) * rstd (+ dresidual_out), kept unrounded (the
+           kernel path rounds once, as the reference's CUDA path and C++ reference do,
+           rmsnorm/csrc/ptx_rmsnorm_kernels.cu:6700-6712);
+      dweight = sum over rows of dout * xhat, in the weight's shape; dbias = sum of dout;
+      sum_abs_* = the same sums of absolute values (the scale the dweight/dbias tolerance
+      is relative to)."""
+    xf = x.cpu().float()
+    r = rstd.cpu().float().unsqueeze(-1)
+    xhat = xf * r
+    g = dout.cpu().float()
+    wdy = g * weight.cpu().float() if weight is not None else g
+    c1 = (xhat * wdy).mean(dim=-1, keepdim=True)
+    dx = (wdy - xhat * c1) * r
+    if dresidual_out is not None:
+        dx = dx + dresidual_out.cpu().float()
+    dw = sdw = None
+    if weight is not None:
+        dw = sum_to_affine_shape(g * xhat, weight.shape)
+        sdw = sum_to_affine_shape((g * xhat).abs(), weight.shape)
+    db = sdb = None
+    if has_bias:
+        shape = bias_shape if bias_shape is not None else (weight.shape if weight is not None else (x.shape[-1],))
+        db = sum_to_affine_shape(g, torch.Size(shape))
+        sdb = sum_to_affine_shape(g.abs(), torch.Size(shape))
+    return dx, dw, db, sdw, sdb
+
+
+def fwd_rows_chunked(x, weight=None, bias=None, residual=None, eps=1e-6, rows=None, chunk=256):
+    """fwd() on a subset of rows of a 2-D problem (rows are independent in the forward),
+    processed in chunks so full-size inputs never need a full-size fp32 temporary."""
+    idx = torch.arange(x.shape[0]) if rows is None else torch.as_tensor(rows)
+    outs, ros, rstds, ys = [], [], [], []
+    for s in range(0, idx.numel(), chunk):
+        sel = idx[s : s + chunk]
+        xs = x[sel].cpu()
+        rs = residual[sel].cpu() if residual is not None else None
+        o, ro, r, y = fwd(xs, weight, bias, rs, eps)
+        outs.append(o); rstds.append(r); ys.append(y)
+        if ro is not None:
+            ros.append(ro)
+    return (torch.cat(outs), torch.cat(ros) if ros else None, torch.cat(rstds), torch.cat(ys))
+
+
+# ---------------------------------------------------------------------------------------
+# Seeded inputs with the BASELINE distributions (x, dy, residual ~ N(0,1); weight ~ N(1, 0.1);
+# bias ~ N(0, 0.02); optional 1% element outliers x100). Generated on the host with a
+# torch.Generator so every machine produces the same tensors.
+# ---------------------------------------------------------------------------------------
+BASE_SEED = 20260514  # the reference harness's default seed (ptx_rmsnorm_kernels.cu:95)
+
+
+def gen(shape, dtype, seed, kind="normal", outliers=0.0):
+    g = torch.Generator().manual_seed(BASE_SEED + seed)
+    t = torch.randn(shape, generator=g, dtype=torch.float32)
+    if kind == "weight":
+        t = 1.0 + 0.1 * t
+    elif kind == "bias":
+        t = 0.02 * t
+    if outliers > 0:
+        mask = torch.rand(shape, generator=g) < outliers
+        t = torch.where(mask, t * 100.0, t)
+    return t.to(dtype)
+
+
+def y_tolerance(dtype: torch.dtype):
+    """y / dx tolerance stated by the task for each dtype: |a - r| <= atol + rtol * |r| with
+    rtol = {bf16: 1.6e-2, fp16: 2e-3, fp32: 1e-5} and atol = rtol * RMS(ref) (absolute
+    floor for values near zero, where a relative bound alone is ill-posed)."""
+    return {torch.bfloat16: 1.6e-2, torch.float16: 2e-3, torch.float32: 1e-5}[dtype]
+
+
+def check_close(actual: Tensor, ref_f32: Tensor, dtype: torch.dtype, label: str, rtol=None):
+    """Asserts |actual - ref| <= rtol * (RMS(ref) + |ref|) elementwise, with the task's
+    per-dtype rtol. `ref_f32` is the unrounded fp32 oracle value; actual is compared after
+    upcasting to fp32. Returns the max normalised error."""
+    rtol = y_tolerance(dtype) if rtol is None else rtol
+    a = actual.detach().cpu().float()
+    r = ref_f32.detach().cpu().float()
+    assert a.shape == r.shape, f"{label}: shape {tuple(a.shape)} != {tuple(r.shape)}"
+    assert torch.isfinite(a).all(), f"{label}: non-finite values"
+    rms = r.square().mean().sqrt().item() if r.numel() else 0.0
+    err = (a - r).abs()
+    bound = rtol * (rms + r.abs())
+    bad = err > bound
+    if bad.any():
+        i = int(bad.flatten().nonzero()[0])
+        raise AssertionError(
+            f"{label}: {int(bad.sum())} of {a.numel()} elements outside tolerance "
+            f"(rtol={rtol}); first at {i}: got {a.flatten()[i].item()} want {r.flatten()[i].item()}"
+        )
+    return float((err / (rms + r.abs() + 1e-30)).max()) if a.numel() else 0.0
+
+
+def check_reduction(actual: Tensor, ref: Tensor, ref_abs: Tensor, label: str, rtol=1e-3):
+    """dweight / dbias bound stated by the task: rtol 1e-3 relative to the fp32 sum, read
+    per column as |a - ref| <= 1e-3 * sum_rows|term| (+1e-6 absolute floor)."""
+    a = actual.detach().cpu().float()
+    r = ref.detach().cpu().float()
+    s = ref_abs.detach().cpu().float()
+    assert a.shape == r.shape, f"{label}: shape {tuple(a.shape)} != {tuple(r.shape)}"
+    err = (a - r).abs()
+    bad = err > rtol * s + 1e-6
+    if bad.any():
+        i = int(bad.flatten().nonzero()[0])
+        raise AssertionError(
+            f"{label}: {int(bad.sum())} of {a.numel()} columns outside tolerance; first at {i}: "
+            f"got {a.flatten()[i].item()} want {r.flatten()[i].item()} (scale {s.flatten()[i].item()})"
+        )
+    return float((err / (s + 1e-30)).max()) if a.numel() else 0.0

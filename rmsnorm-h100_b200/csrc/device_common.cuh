@@ -1,0 +1,385 @@
+// device_common.cuh -- sm_100a building blocks shared by every kernel of the library:
+// inline-PTX wrappers for mbarriers, TMA bulk copies (cp.async.bulk, no tensor map, no
+// multicast), cluster / distributed-shared-memory access, bounded waits that report
+// through a device status word, and dtype-generic 8-element vector load/store.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "rmsnorm_b200.h"
+
+namespace rmsb200 {
+
+// ---------------------------------------------------------------------------------------
+// Device status word (one per device: file-scope __device__ variables live in each
+// device's copy of the module). 0 = OK; otherwise the first error recorded. The library
+// is a single translation unit, so the variables are defined here.
+// ---------------------------------------------------------------------------------------
+__device__ int g_status = 0;
+__device__ int g_status_where = 0;
+__device__ unsigned long long g_wait_timeout_ns = 2000000000ull;
+
+// Where a bounded wait gave up (reported through rmsnorm_b200_device_status).
+enum WaitSite : int {
+  kSiteFwdFull = 1,
+  kSiteFwdEmpty = 2,
+  kSiteFwdCluster = 3,
+  kSiteBwdFull = 4,
+  kSiteBwdEmpty = 5,
+  kSiteBwdCluster = 6,
+  kSiteDrain = 7,
+  kSiteSelftest = 8,
+};
+
+__device__ __forceinline__ void record_error(int code, int where) {
+  if (atomicCAS(&g_status, 0, code) == 0) {
+    atomicExch(&g_status_where, where);
+  }
+}
+
+__device__ __forceinline__ bool abort_requested() {
+  return *reinterpret_cast<volatile int*>(&g_status) != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------------------
+// Shared-memory addresses, mbarriers
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+// Makes mbarrier initialisation visible to the async proxy and to the other CTAs of
+// the cluster.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// One probe of phase `parity`; the hardware may suspend the thread for a short while.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Same, with cluster-scope acquire: used where peers of the cluster complete the phase
+// with st.async ... complete_tx into this CTA's shared memory.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (after recording the error) when the phase has not
+// completed within g_wait_timeout_ns, or as soon as another thread of any CTA has
+// recorded an error.
+template <bool kClusterScope = false>
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int where) {
+  if (kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) {
+    return true;
+  }
+  const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = g_wait_timeout_ns;
+  uint32_t spins = 0;
+  while (true) {
+    if (kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) {
+      return true;
+    }
+    if ((++spins & 15u) == 0u) {
+      if (abort_requested()) return false;
+      if (globaltimer_ns() - t0 > limit) {
+        record_error(RMSNORM_B200_ERR_DEVICE_TIMEOUT, where);
+        return false;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// TMA bulk copy (global -> this CTA's shared memory), completion counted in bytes on an
+// mbarrier. Source and destination 16-byte aligned, size a multiple of 16. No multicast.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// Orders this CTA's earlier generic-proxy accesses to shared memory before later
+// async-proxy (TMA) writes to it: issued before a stage is refilled.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                          uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Non-bulk async copy of 4 or 16 bytes; completion is attached to an mbarrier with
+// cp_async_arrive (which raises the barrier's expected arrivals by one first, so the
+// phase cannot complete before these copies land).
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// Clusters / distributed shared memory
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+
+// All threads of all CTAs of the cluster. Used once, at kernel start, so that every
+// CTA's mbarriers are initialised before any peer signals them.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+
+__device__ __forceinline__ uint32_t map_peer(uint32_t local_smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
+  return r;
+}
+
+// 4-byte store into a peer CTA's shared memory that completes 4 tx-bytes on the peer's
+// mbarrier (the peer waits for the bytes, not for an arrival).
+__device__ __forceinline__ void st_async_peer(uint32_t remote_addr, float v, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
+          remote_addr),
+      "r"(__float_as_uint(v)), "r"(remote_bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void named_barrier(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// 8-element vectors. Every tensor of a row is handled in groups of 8 consecutive
+// elements: 16 bytes for fp16/bf16, 32 bytes for fp32.
+// ---------------------------------------------------------------------------------------
+template <typename T>
+struct Vec8;
+
+template <>
+struct Vec8<float> {
+  static constexpr int kBytes = 32;
+  __device__ __forceinline__ static void load(const void* p, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0];
+    const float4 b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  __device__ __forceinline__ static void load_global(const void* p, float (&v)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  __device__ __forceinline__ static void store(void* p, const float (&v)[8]) {
+    __stcs(reinterpret_cast<float4*>(p), make_float4(v[0], v[1], v[2], v[3]));
+    __stcs(reinterpret_cast<float4*>(p) + 1, make_float4(v[4], v[5], v[6], v[7]));
+  }
+};
+
+__device__ __forceinline__ void unpack_bf16x2(uint32_t u, float& lo, float& hi) {
+  lo = __uint_as_float(u << 16);
+  hi = __uint_as_float(u & 0xffff0000u);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void unpack_f16x2(uint32_t u, float& lo, float& hi) {
+  __half2 h = *reinterpret_cast<__half2*>(&u);
+  float2 f = __half22float2(h);
+  lo = f.x;
+  hi = f.y;
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <>
+struct Vec8<__nv_bfloat16> {
+  static constexpr int kBytes = 16;
+  __device__ __forceinline__ static void unpack(const uint4 u, float (&v)[8]) {
+    unpack_bf16x2(u.x, v[0], v[1]);
+    unpack_bf16x2(u.y, v[2], v[3]);
+    unpack_bf16x2(u.z, v[4], v[5]);
+    unpack_bf16x2(u.w, v[6], v[7]);
+  }
+  __device__ __forceinline__ static void load(const void* p, float (&v)[8]) {
+    unpack(*reinterpret_cast<const uint4*>(p), v);
+  }
+  __device__ __forceinline__ static void load_global(const void* p, float (&v)[8]) {
+    unpack(__ldg(reinterpret_cast<const uint4*>(p)), v);
+  }
+  __device__ __forceinline__ static void store(void* p, const float (&v)[8]) {
+    uint4 u;
+    u.x = pack_bf16x2(v[0], v[1]);
+    u.y = pack_bf16x2(v[2], v[3]);
+    u.z = pack_bf16x2(v[4], v[5]);
+    u.w = pack_bf16x2(v[6], v[7]);
+    __stcs(reinterpret_cast<uint4*>(p), u);
+  }
+};
+
+template <>
+struct Vec8<__half> {
+  static constexpr int kBytes = 16;
+  __device__ __forceinline__ static void unpack(const uint4 u, float (&v)[8]) {
+    unpack_f16x2(u.x, v[0], v[1]);
+    unpack_f16x2(u.y, v[2], v[3]);
+    unpack_f16x2(u.z, v[4], v[5]);
+    unpack_f16x2(u.w, v[6], v[7]);
+  }
+  __device__ __forceinline__ static void load(const void* p, float (&v)[8]) {
+    unpack(*reinterpret_cast<const uint4*>(p), v);
+  }
+  __device__ __forceinline__ static void load_global(const void* p, float (&v)[8]) {
+    unpack(__ldg(reinterpret_cast<const uint4*>(p)), v);
+  }
+  __device__ __forceinline__ static void store(void* p, const float (&v)[8]) {
+    uint4 u;
+    u.x = pack_f16x2(v[0], v[1]);
+    u.y = pack_f16x2(v[2], v[3]);
+    u.z = pack_f16x2(v[4], v[5]);
+    u.w = pack_f16x2(v[6], v[7]);
+    __stcs(reinterpret_cast<uint4*>(p), u);
+  }
+};
+
+// Runtime-dtype variants for tensors whose dtype is not a template parameter (outputs
+// of secondary dtype, affine parameters loaded once). `e` is the element index.
+__device__ __forceinline__ int dtype_bytes(int dt) { return dt == RMSNORM_B200_F32 ? 4 : 2; }
+
+__device__ __forceinline__ void load8_rt(const void* base, int dt, int64_t e, float (&v)[8],
+                                         bool global) {
+  if (dt == RMSNORM_B200_F32) {
+    const float* p = reinterpret_cast<const float*>(base) + e;
+    if (global) Vec8<float>::load_global(p, v); else Vec8<float>::load(p, v);
+  } else if (dt == RMSNORM_B200_BF16) {
+    const __nv_bfloat16* p = reinterpret_cast<const __nv_bfloat16*>(base) + e;
+    if (global) Vec8<__nv_bfloat16>::load_global(p, v); else Vec8<__nv_bfloat16>::load(p, v);
+  } else {
+    const __half* p = reinterpret_cast<const __half*>(base) + e;
+    if (global) Vec8<__half>::load_global(p, v); else Vec8<__half>::load(p, v);
+  }
+}
+
+__device__ __forceinline__ void store8_rt(void* base, int dt, int64_t e, const float (&v)[8]) {
+  if (dt == RMSNORM_B200_F32) {
+    Vec8<float>::store(reinterpret_cast<float*>(base) + e, v);
+  } else if (dt == RMSNORM_B200_BF16) {
+    Vec8<__nv_bfloat16>::store(reinterpret_cast<__nv_bfloat16*>(base) + e, v);
+  } else {
+    Vec8<__half>::store(reinterpret_cast<__half*>(base) + e, v);
+  }
+}
+
+// Scalar runtime-dtype access (generic kernels).
+__device__ __forceinline__ float load1_rt(const void* base, int dt, int64_t e) {
+  if (dt == RMSNORM_B200_F32) return reinterpret_cast<const float*>(base)[e];
+  if (dt == RMSNORM_B200_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[e]);
+  return __half2float(reinterpret_cast<const __half*>(base)[e]);
+}
+
+__device__ __forceinline__ void store1_rt(void* base, int dt, int64_t e, float v) {
+  if (dt == RMSNORM_B200_F32) {
+    reinterpret_cast<float*>(base)[e] = v;
+  } else if (dt == RMSNORM_B200_BF16) {
+    reinterpret_cast<__nv_bfloat16*>(base)[e] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<__half*>(base)[e] = __float2half_rn(v);
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+}  // namespace rmsb200

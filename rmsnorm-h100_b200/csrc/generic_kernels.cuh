@@ -1,0 +1,163 @@
+// generic_kernels.cuh -- kernels for every case the streaming kernels do not take:
+// hidden sizes that are not a multiple of 8, pointers that are not 16-byte aligned,
+// dtype combinations outside the specialised set, per-head segments whose length is not
+// a power of two <= 32 vectors, and rows too long for the cluster split. They compute
+// the same fp32 math with scalar runtime-typed loads (one CTA per row, grid-stride) and
+// keep dweight/dbias deterministic with fixed-order chunked column sums.
+#pragma once
+
+#include "device_common.cuh"
+
+namespace rmsb200 {
+
+constexpr int kGenericThreads = 256;
+
+struct GenFwdParams {
+  int64_t rows, N;
+  int32_t H;
+  const void* x; int32_t x_dt;
+  const void* res; int32_t res_dt;
+  const void* w; int32_t w_dt, w_ph;
+  const void* b; int32_t b_dt, b_ph;
+  void* out; int32_t out_dt;
+  void* ro; int32_t ro_dt;
+  float* rstd;
+  float eps;
+};
+
+struct GenBwdParams {
+  int64_t rows, N;
+  int32_t H;
+  const void* x; int32_t x_dt;
+  const void* dy; int32_t dy_dt;
+  const float* rstd;
+  const void* w; int32_t w_dt, w_ph;
+  const void* dro; int32_t dro_dt;
+  void* dx; int32_t dx_dt;
+  void* dres; int32_t dres_dt;
+};
+
+// Block-wide sum, summed in warp order so every thread gets the same bits.
+__device__ __forceinline__ float block_sum_fixed(float v, float* red) {
+  v = warp_sum(v);
+  const int nw = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int j = 0; j < nw; ++j) t += red[j];
+  __syncthreads();
+  return t;
+}
+
+__global__ void __launch_bounds__(kGenericThreads) fwd_generic_kernel(const GenFwdParams p) {
+  __shared__ float red[32];
+  const int64_t N = p.N;
+  for (int64_t r = blockIdx.x; r < p.rows; r += gridDim.x) {
+    const int64_t base = r * N;
+    const int64_t head = r % p.H;
+    float acc = 0.f;
+    for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+      float v = load1_rt(p.x, p.x_dt, base + n);
+      if (p.res) v += load1_rt(p.res, p.res_dt, base + n);
+      acc = fmaf(v, v, acc);
+    }
+    acc = block_sum_fixed(acc, red);
+    const float rs = rsqrtf(acc / static_cast<float>(N) + p.eps);
+    for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+      float v = load1_rt(p.x, p.x_dt, base + n);
+      if (p.res) v += load1_rt(p.res, p.res_dt, base + n);
+      if (p.ro) store1_rt(p.ro, p.ro_dt, base + n, v);
+      const float w = p.w ? load1_rt(p.w, p.w_dt, (p.w_ph ? head * N : 0) + n) : 1.f;
+      const float b = p.b ? load1_rt(p.b, p.b_dt, (p.b_ph ? head * N : 0) + n) : 0.f;
+      store1_rt(p.out, p.out_dt, base + n, fmaf(v * rs, w, b));
+    }
+    if (threadIdx.x == 0 && p.rstd) p.rstd[r] = rs;
+  }
+}
+
+__global__ void __launch_bounds__(kGenericThreads) bwd_generic_dx_kernel(const GenBwdParams p) {
+  __shared__ float red[32];
+  const int64_t N = p.N;
+  for (int64_t r = blockIdx.x; r < p.rows; r += gridDim.x) {
+    const int64_t base = r * N;
+    const int64_t woff = p.w_ph ? (r % p.H) * N : 0;
+    const float rs = p.rstd[r];
+    float acc = 0.f;
+    for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+      const float xh = load1_rt(p.x, p.x_dt, base + n) * rs;
+      const float w = p.w ? load1_rt(p.w, p.w_dt, woff + n) : 1.f;
+      acc = fmaf(xh, load1_rt(p.dy, p.dy_dt, base + n) * w, acc);
+    }
+    acc = block_sum_fixed(acc, red);
+    const float c = acc / static_cast<float>(N);
+    for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+      const float xh = load1_rt(p.x, p.x_dt, base + n) * rs;
+      const float w = p.w ? load1_rt(p.w, p.w_dt, woff + n) : 1.f;
+      float g = (load1_rt(p.dy, p.dy_dt, base + n) * w - xh * c) * rs;
+      if (p.dro) g += load1_rt(p.dro, p.dro_dt, base + n);
+      store1_rt(p.dx, p.dx_dt, base + n, g);
+      if (p.dres) store1_rt(p.dres, p.dres_dt, base + n, g);
+    }
+  }
+}
+
+// partial[chunk][j] = sum over super-rows t of chunk (in order) of dout * xhat (and dout),
+// for super-row column j in [0, H*N). Row of (t, j) is t*H + j/N.
+__global__ void __launch_bounds__(kGenericThreads) bwd_generic_partials_kernel(
+    const GenBwdParams p, int64_t chunk_rows, float* dw_part, float* db_part) {
+  const int64_t W = p.N * p.H;
+  const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (j >= W) return;
+  const int64_t nsup = p.rows / p.H;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.y) * chunk_rows;
+  const int64_t t1 = min(nsup, t0 + chunk_rows);
+  const int64_t head = j / p.N;
+  float dw = 0.f, db = 0.f;
+  for (int64_t t = t0; t < t1; ++t) {
+    const int64_t e = t * W + j;
+    const float dy = load1_rt(p.dy, p.dy_dt, e);
+    const float xh = load1_rt(p.x, p.x_dt, e) * p.rstd[t * p.H + head];
+    dw = fmaf(dy, xh, dw);
+    db += dy;
+  }
+  if (dw_part) dw_part[static_cast<int64_t>(blockIdx.y) * W + j] = dw;
+  if (db_part) db_part[static_cast<int64_t>(blockIdx.y) * W + j] = db;
+}
+
+// out[j] = sum_{c < C} sum_{h < fold} part[c][h * N + j], in exactly that order.
+// fold = H folds a per-head super-row back onto a shared [N] parameter; fold = 1 keeps
+// all W = H*N columns.
+__global__ void __launch_bounds__(kGenericThreads) reduce_partials_kernel(
+    const float* __restrict__ part, int64_t C, int64_t W, int64_t N, int32_t fold,
+    void* out, int32_t out_dt) {
+  const int64_t wout = fold > 1 ? N : W;
+  const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (j >= wout) return;
+  float acc = 0.f;
+  for (int64_t c = 0; c < C; ++c) {
+    const float* row = part + c * W;
+    for (int h = 0; h < fold; ++h) acc += row[h * N + j];
+  }
+  store1_rt(out, out_dt, j, acc);
+}
+
+// Failure-detection self test: one CTA waits on an mbarrier that nothing arrives at.
+__global__ void selftest_wait_kernel(unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(&bar, 0)) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        record_error(RMSNORM_B200_ERR_DEVICE_TIMEOUT, kSiteSelftest);
+        break;
+      }
+    }
+  }
+}
+
+}  // namespace rmsb200

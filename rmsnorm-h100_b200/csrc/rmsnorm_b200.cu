@@ -1,0 +1,651 @@
+// rmsnorm_b200.cu -- C ABI, per-device state, launch planner and dispatch.
+//
+// Dispatch (replaces launch_fwd / launch_bwd of the reference,
+// rmsnorm/csrc/ptx_rmsnorm_kernels.cu:4941-6600, and its per-(dtype, N) thread tables):
+//   * streaming kernels (stream_kernels.cuh) for every shape whose rows are 8-element
+//     vectorisable and 16-byte aligned, in the specialised dtype set;
+//   * generic kernels (generic_kernels.cuh) for everything else;
+//   * backward dweight/dbias: per-(CTA, row group) fp32 partial rows written by the main
+//     kernel, summed in a fixed order by reduce_partials_kernel (deterministic; the
+//     reference used fp32 atomics on several paths, ptx_rmsnorm_kernels.cu:3288-3291).
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "generic_kernels.cuh"
+#include "stream_kernels.cuh"
+
+namespace rmsb200 {
+
+namespace {
+
+std::atomic<uint64_t> g_launches{0};
+thread_local std::string t_last_plan;
+
+constexpr int kSmemBudget = 232448 - kSmemReserve;  // 227 KB opt-in minus barrier area
+
+int elem_bytes(int dt) { return dt == RMSNORM_B200_F32 ? 4 : 2; }
+bool valid_dt(int dt) { return dt == RMSNORM_B200_F16 || dt == RMSNORM_B200_BF16 || dt == RMSNORM_B200_F32; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------------------------------
+// Per-device state: SM count, kernel attributes set once per (device, kernel), cached
+// occupancy queries. Kernel attributes are per device, so they are set lazily for each
+// device a call runs on (the reference set them once per process, which is wrong with
+// more than one GPU: ptx_rmsnorm_kernels.cu:5471-5475).
+// ------------------------------------------------------------------------------------
+struct DeviceState {
+  int sm_count = 0;
+  std::mutex mu;
+  std::map<const void*, bool> attrs_done;
+  std::map<std::tuple<const void*, int, int>, int> occupancy;  // (kernel, P, smem) -> clusters or blocks/SM
+};
+
+std::mutex g_devices_mu;
+std::vector<std::unique_ptr<DeviceState>> g_devices;
+
+int get_device_state(DeviceState** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return RMSNORM_B200_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_devices_mu);
+  if (static_cast<int>(g_devices.size()) <= dev) g_devices.resize(dev + 1);
+  if (!g_devices[dev]) {
+    auto st = std::make_unique<DeviceState>();
+    if (cudaDeviceGetAttribute(&st->sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return RMSNORM_B200_ERR_NO_DEVICE;
+    g_devices[dev] = std::move(st);
+  }
+  *out = g_devices[dev].get();
+  return RMSNORM_B200_OK;
+}
+
+int ensure_attrs(DeviceState* ds, const void* kernel, int smem) {
+  std::lock_guard<std::mutex> lock(ds->mu);
+  if (ds->attrs_done.count(kernel)) return RMSNORM_B200_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448) != cudaSuccess)
+    return RMSNORM_B200_ERR_CUDA;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+    return RMSNORM_B200_ERR_CUDA;
+  (void)smem;
+  ds->attrs_done[kernel] = true;
+  return RMSNORM_B200_OK;
+}
+
+// Clusters of P CTAs (P > 1) or CTAs per SM (P == 1) that can be resident at once.
+int resident_units(DeviceState* ds, const void* kernel, int P, int smem) {
+  {
+    std::lock_guard<std::mutex> lock(ds->mu);
+    auto it = ds->occupancy.find(std::make_tuple(kernel, P, smem));
+    if (it != ds->occupancy.end()) return it->second;
+  }
+  int n = 0;
+  if (P == 1) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kBlockThreads, smem) != cudaSuccess) n = 0;
+    n *= ds->sm_count;
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(P * ds->sm_count);
+    cfg.blockDim = dim3(kBlockThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = P;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();  // a refused query must not poison the caller's next check
+  std::lock_guard<std::mutex> lock(ds->mu);
+  ds->occupancy[std::make_tuple(kernel, P, smem)] = n;
+  return n;
+}
+
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return v ? std::atoi(v) : dflt;
+}
+
+int pow2_ceil(int v) {
+  int p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+bool is_pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
+
+uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+// Builds the thread/tile/stage/cluster plan for a streaming kernel. `in_bytes[k]` is the
+// element size of staged input k (0 = absent); `rstd_staged` adds the per-row rstd block
+// (backward). Returns false (with a reason) when the shape is outside what the streaming
+// kernels take.
+bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], bool rstd_staged,
+                      int max_vecs, StreamPlan* out, std::string* why) {
+  StreamPlan pl = {};
+  if (N64 % 8 != 0 || N64 > (int64_t(1) << 30)) { *why = "hidden % 8 != 0"; return false; }
+  const int N = static_cast<int>(N64);
+  const int64_t W = static_cast<int64_t>(H) * N;
+  if (W / 8 > (int64_t(1) << 24)) { *why = "row too long"; return false; }
+  const int vrow = static_cast<int>(W / 8);
+  const int T = kConsumerThreads;
+  pl.T = T;
+  pl.heads = H;
+  pl.N = N;
+  pl.W = W;
+  pl.nrows = rows / H;
+  int P = 1;
+  if (H > 1) {
+    const int vs = N / 8;
+    if (!is_pow2(vs) || vs > 32) { *why = "per-head segment not a power of two <= 32 vectors"; return false; }
+    const int per_thread_min = (vrow + max_vecs - 1) / max_vecs;
+    const int G = vs * ((per_thread_min + vs - 1) / vs);
+    if (G > T) { *why = "per-head super-row too wide"; return false; }
+    pl.seg_mode = 1;
+    pl.vs = vs;
+    pl.G = G;
+    pl.vslice = vrow;
+  } else if (vrow <= 32) {
+    pl.seg_mode = 1;
+    pl.vs = pow2_ceil(vrow);
+    pl.G = pl.vs;
+    pl.vslice = vrow;
+  } else {
+    pl.seg_mode = 0;
+    pl.vs = 0;
+    int bytes_per_vec = 0;
+    for (int k = 0; k < 3; ++k) bytes_per_vec += 8 * in_bytes[k];
+    const int max_p = std::min(kMaxCluster, env_int("RMSNORM_B200_MAX_CLUSTER", kMaxCluster));
+    const int force_p = env_int("RMSNORM_B200_FORCE_CLUSTER", 0);
+    P = 0;
+    for (int cand = 1; cand <= max_p; cand <<= 1) {
+      if (force_p && cand != force_p) continue;
+      if (vrow % cand) continue;
+      const int vs_ = vrow / cand;
+      if (vs_ > T * max_vecs) continue;
+      const int64_t slice_bytes = static_cast<int64_t>(vs_) * bytes_per_vec + (rstd_staged ? 16 : 0);
+      if (slice_bytes > kSmemBudget) continue;
+      // prefer a split that leaves room for at least two stages
+      if (slice_bytes * 2 > kSmemBudget && cand < max_p && !force_p &&
+          vrow % (cand * 2) == 0 && (vrow / (cand * 2)) >= 32)
+        continue;
+      P = cand;
+      break;
+    }
+    if (P == 0) { *why = "no cluster split fits"; return false; }
+    pl.vslice = vrow / P;
+    const int per_thread_min = (pl.vslice + max_vecs - 1) / max_vecs;
+    pl.G = std::min(T, static_cast<int>(align_up(static_cast<uint32_t>(per_thread_min), 32u)));
+  }
+  pl.P = P;
+  pl.rps = P > 1 ? 1 : T / pl.G;
+  if (pl.rps < 1) { *why = "group wider than the CTA"; return false; }
+
+  uint32_t per_row = 0;
+  for (int k = 0; k < 3; ++k) {
+    pl.row_bytes[k] = static_cast<uint32_t>(pl.vslice) * 8u * in_bytes[k];
+    per_row += pl.row_bytes[k];
+  }
+  const int rstd_per_row = pl.seg_mode ? H : 1;
+  if (rstd_staged) per_row += 4u * rstd_per_row;
+  const int target = env_int("RMSNORM_B200_STAGE_BYTES", 48 * 1024);
+  int R = pl.rps;
+  if (P == 1) {
+    const int64_t m = std::max<int64_t>(1, target / (static_cast<int64_t>(pl.rps) * per_row));
+    R = static_cast<int>(pl.rps * m);
+    const int64_t rows_needed = (pl.nrows + pl.rps - 1) / pl.rps * pl.rps;
+    if (R > rows_needed) R = static_cast<int>(std::max<int64_t>(pl.rps, rows_needed));
+  }
+  auto layout = [&](int r) {
+    uint32_t off = 0;
+    for (int k = 0; k < 3; ++k) {
+      pl.off[k] = off;
+      off = align_up(off + static_cast<uint32_t>(r) * pl.row_bytes[k], 128);
+    }
+    pl.off[3] = off;
+    if (rstd_staged) off = align_up(off + 4u * r * rstd_per_row, 128);
+    return off;
+  };
+  uint32_t stage = layout(R);
+  while (stage > static_cast<uint32_t>(kSmemBudget) && R > pl.rps) {
+    R -= pl.rps;
+    stage = layout(R);
+  }
+  if (stage > static_cast<uint32_t>(kSmemBudget)) { *why = "stage does not fit shared memory"; return false; }
+  pl.R = R;
+  pl.stage_bytes = stage;
+  const int max_s = std::max(1, std::min(kMaxStages, env_int("RMSNORM_B200_MAX_STAGES", kMaxStages)));
+  pl.S = std::max(1, std::min<int>(max_s, kSmemBudget / stage));
+  pl.ntiles = (pl.nrows + R - 1) / R;
+  *out = pl;
+  return true;
+}
+
+int smem_bytes(const StreamPlan& pl) { return pl.S * static_cast<int>(pl.stage_bytes) + kSmemReserve; }
+
+std::string describe(const char* kind, const StreamPlan& pl, int grid) {
+  char buf[512];
+  std::snprintf(buf, sizeof(buf),
+                "%s mode=%s P=%d grid=%d clusters=%d T=%d G=%d rps=%d R=%d S=%d stage=%u "
+                "vslice=%d vs=%d tiles=%lld",
+                kind, pl.seg_mode ? "seg" : "row", pl.P, grid, pl.nclusters, pl.T, pl.G, pl.rps,
+                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, static_cast<long long>(pl.ntiles));
+  return buf;
+}
+
+template <typename Params>
+int launch_stream(DeviceState* ds, void (*kernel)(const Params), Params params, StreamPlan& pl,
+                  cudaStream_t stream, const char* kind, bool dry_run, int* grid_out) {
+  const int smem = smem_bytes(pl);
+  if (ensure_attrs(ds, reinterpret_cast<const void*>(kernel), smem) != RMSNORM_B200_OK)
+    return RMSNORM_B200_ERR_CUDA;
+  const int units = resident_units(ds, reinterpret_cast<const void*>(kernel), pl.P, smem);
+  if (units <= 0) return RMSNORM_B200_ERR_UNSUPPORTED;
+  const int64_t nclusters = std::min<int64_t>(pl.ntiles, units);
+  pl.nclusters = static_cast<int>(nclusters);
+  const int grid = static_cast<int>(nclusters * pl.P);
+  if (grid_out) *grid_out = grid;
+  if (dry_run) return RMSNORM_B200_OK;
+  params.pl = pl;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kBlockThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = pl.P;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pl.P > 1 ? 1 : 0;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, params);
+  if (err != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  t_last_plan = describe(kind, pl, grid);
+  return RMSNORM_B200_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// Kernel tables
+// ---------------------------------------------------------------------------------------
+using FwdKernel = void (*)(const FwdParams);
+using BwdKernel = void (*)(const BwdParams);
+
+FwdKernel pick_fwd(int x_dt, int r_dt) {
+  // r_dt: dtype of the residual (equal to x_dt when there is none)
+  if (x_dt == RMSNORM_B200_BF16 && r_dt == RMSNORM_B200_BF16) return fwd_stream_kernel<__nv_bfloat16, __nv_bfloat16>;
+  if (x_dt == RMSNORM_B200_F16 && r_dt == RMSNORM_B200_F16) return fwd_stream_kernel<__half, __half>;
+  if (x_dt == RMSNORM_B200_F32 && r_dt == RMSNORM_B200_F32) return fwd_stream_kernel<float, float>;
+  if (x_dt == RMSNORM_B200_BF16 && r_dt == RMSNORM_B200_F32) return fwd_stream_kernel<__nv_bfloat16, float>;
+  if (x_dt == RMSNORM_B200_F16 && r_dt == RMSNORM_B200_F32) return fwd_stream_kernel<__half, float>;
+  return nullptr;
+}
+
+// Vectors per thread: the dbias variants keep a third register array, so they own two
+// vectors per super-row slice instead of four to stay within 128 registers.
+constexpr int kBwdVecsDb = 2;
+int bwd_max_vecs(bool has_db) { return has_db ? kBwdVecsDb : kMaxVecs; }
+
+BwdKernel pick_bwd(int x_dt, int dy_dt, bool has_db) {
+#define RMSB_BWD(XT, DT, XC, DC)                                                          \
+  if (x_dt == XC && dy_dt == DC)                                                          \
+    return has_db ? bwd_stream_kernel<XT, DT, true, kBwdVecsDb> : bwd_stream_kernel<XT, DT, false, kMaxVecs>;
+  RMSB_BWD(__nv_bfloat16, __nv_bfloat16, RMSNORM_B200_BF16, RMSNORM_B200_BF16)
+  RMSB_BWD(__half, __half, RMSNORM_B200_F16, RMSNORM_B200_F16)
+  RMSB_BWD(float, float, RMSNORM_B200_F32, RMSNORM_B200_F32)
+  RMSB_BWD(float, __nv_bfloat16, RMSNORM_B200_F32, RMSNORM_B200_BF16)
+  RMSB_BWD(float, __half, RMSNORM_B200_F32, RMSNORM_B200_F16)
+#undef RMSB_BWD
+  return nullptr;
+}
+
+// ---------------------------------------------------------------------------------------
+// Argument validation
+// ---------------------------------------------------------------------------------------
+int check_common(int64_t rows, int64_t hidden, int heads) {
+  if (rows < 0 || hidden < 1 || heads < 1) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (rows % heads != 0) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  return RMSNORM_B200_OK;
+}
+
+int check_fwd(const rmsnorm_b200_fwd_args* a) {
+  if (!a) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  int st = check_common(a->rows, a->hidden, a->heads);
+  if (st) return st;
+  if (!a->x || !a->out || !valid_dt(a->x_dtype) || !valid_dt(a->out_dtype))
+    return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->residual && !valid_dt(a->residual_dtype)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->residual_out && !valid_dt(a->residual_out_dtype)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->weight && (!valid_dt(a->weight_dtype) || (a->weight_heads != 1 && a->weight_heads != a->heads)))
+    return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->bias && (!valid_dt(a->bias_dtype) || (a->bias_heads != 1 && a->bias_heads != a->heads)))
+    return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->heads > 1) {
+    const bool wh = a->weight && a->weight_heads == a->heads;
+    const bool bh = a->bias && a->bias_heads == a->heads;
+    if (!wh && !bh) return RMSNORM_B200_ERR_INVALID_ARGUMENT;  // heads only come from an affine tensor
+  }
+  return RMSNORM_B200_OK;
+}
+
+int check_bwd(const rmsnorm_b200_bwd_args* a) {
+  if (!a) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  int st = check_common(a->rows, a->hidden, a->heads);
+  if (st) return st;
+  if (!a->x || !a->dout || !a->rstd || !a->dx) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (!valid_dt(a->x_dtype) || !valid_dt(a->dout_dtype) || !valid_dt(a->dx_dtype))
+    return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->weight && (!valid_dt(a->weight_dtype) || (a->weight_heads != 1 && a->weight_heads != a->heads)))
+    return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->dweight && (!a->weight || !valid_dt(a->dweight_dtype))) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->dbias && (!valid_dt(a->dbias_dtype) || (a->dbias_heads != 1 && a->dbias_heads != a->heads)))
+    return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->dresidual_out && !valid_dt(a->dresidual_out_dtype)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->dresidual && !valid_dt(a->dresidual_dtype)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  return RMSNORM_B200_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// Forward
+// ---------------------------------------------------------------------------------------
+bool fwd_stream_eligible(const rmsnorm_b200_fwd_args* a, std::string* why) {
+  if (a->hidden % 8) { *why = "hidden % 8"; return false; }
+  const void* ptrs[] = {a->x, a->residual, a->weight, a->bias, a->out, a->residual_out};
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) { *why = "unaligned pointer"; return false; }
+  const int r_dt = a->residual ? a->residual_dtype : a->x_dtype;
+  if (!pick_fwd(a->x_dtype, r_dt)) { *why = "dtype combination"; return false; }
+  return true;
+}
+
+int launch_fwd_generic(DeviceState* ds, const rmsnorm_b200_fwd_args* a, cudaStream_t stream,
+                       const std::string& why) {
+  GenFwdParams g = {};
+  g.rows = a->rows; g.N = a->hidden; g.H = a->heads;
+  g.x = a->x; g.x_dt = a->x_dtype;
+  g.res = a->residual; g.res_dt = a->residual_dtype;
+  g.w = a->weight; g.w_dt = a->weight_dtype; g.w_ph = a->weight && a->weight_heads > 1;
+  g.b = a->bias; g.b_dt = a->bias_dtype; g.b_ph = a->bias && a->bias_heads > 1;
+  g.out = a->out; g.out_dt = a->out_dtype;
+  g.ro = a->residual_out; g.ro_dt = a->residual_out_dtype;
+  g.rstd = a->rstd; g.eps = a->eps;
+  const int64_t grid = std::min<int64_t>(a->rows, static_cast<int64_t>(ds->sm_count) * 8);
+  fwd_generic_kernel<<<static_cast<unsigned>(grid), kGenericThreads, 0, stream>>>(g);
+  if (cudaGetLastError() != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  t_last_plan = "fwd_generic (" + why + ") grid=" + std::to_string(grid);
+  return RMSNORM_B200_OK;
+}
+
+int do_fwd(const rmsnorm_b200_fwd_args* a, cudaStream_t stream) {
+  int st = check_fwd(a);
+  if (st) return st;
+  if (a->rows == 0) { t_last_plan = "fwd empty"; return RMSNORM_B200_OK; }
+  DeviceState* ds = nullptr;
+  st = get_device_state(&ds);
+  if (st) return st;
+  std::string why;
+  const bool force_generic = env_int("RMSNORM_B200_FORCE_GENERIC", 0) != 0;
+  if (!force_generic && fwd_stream_eligible(a, &why)) {
+    StreamPlan pl;
+    const int r_dt = a->residual ? a->residual_dtype : a->x_dtype;
+    const int in_bytes[3] = {elem_bytes(a->x_dtype), a->residual ? elem_bytes(r_dt) : 0, 0};
+    if (make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, false, kMaxVecs, &pl, &why)) {
+      FwdParams p = {};
+      p.x = a->x; p.res = a->residual; p.w = a->weight; p.b = a->bias;
+      p.out = a->out; p.ro = a->residual_out; p.rstd = a->rstd;
+      p.w_dt = a->weight_dtype; p.b_dt = a->bias_dtype; p.out_dt = a->out_dtype;
+      p.ro_dt = a->residual_out_dtype;
+      p.w_per_head = a->weight && a->weight_heads > 1;
+      p.b_per_head = a->bias && a->bias_heads > 1;
+      p.eps = a->eps;
+      st = launch_stream(ds, pick_fwd(a->x_dtype, r_dt), p, pl, stream, "fwd_stream", false, nullptr);
+      if (st != RMSNORM_B200_ERR_UNSUPPORTED) return st;
+      why = "cluster not schedulable";
+    }
+  } else if (force_generic) {
+    why = "forced";
+  }
+  return launch_fwd_generic(ds, a, stream, why);
+}
+
+// ---------------------------------------------------------------------------------------
+// Backward
+// ---------------------------------------------------------------------------------------
+struct BwdPlan {
+  bool stream = false;
+  StreamPlan pl = {};
+  BwdKernel kernel = nullptr;
+  int grid = 0;
+  int64_t nparts = 0;        // partial rows per requested gradient
+  int64_t chunk_rows = 0;    // generic: super-rows per chunk
+  int64_t W = 0;
+  bool need_dw = false, need_db = false;
+  std::string why;
+};
+
+int plan_bwd(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdPlan* bp) {
+  bp->W = a->hidden * a->heads;
+  bp->need_dw = a->dweight != nullptr;
+  bp->need_db = a->dbias != nullptr;
+  std::string why;
+  bool ok = env_int("RMSNORM_B200_FORCE_GENERIC", 0) == 0;
+  if (!ok) why = "forced";
+  if (ok && a->hidden % 8) { ok = false; why = "hidden % 8"; }
+  if (ok) {
+    const void* ptrs[] = {a->x, a->dout, a->weight, a->dresidual_out, a->dx, a->dresidual};
+    for (const void* p : ptrs)
+      if (p && !aligned16(p)) { ok = false; why = "unaligned pointer"; }
+  }
+  if (ok && a->dx_dtype != a->dout_dtype) { ok = false; why = "dx dtype != dout dtype"; }
+  if (ok) {
+    bp->kernel = pick_bwd(a->x_dtype, a->dout_dtype, bp->need_db);
+    if (!bp->kernel) { ok = false; why = "dtype combination"; }
+  }
+  if (ok) {
+    const int in_bytes[3] = {elem_bytes(a->x_dtype), elem_bytes(a->dout_dtype),
+                             a->dresidual_out ? elem_bytes(a->dresidual_out_dtype) : 0};
+    StreamPlan pl;
+    if (make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, true, bwd_max_vecs(bp->need_db), &pl,
+                         &why)) {
+      int grid = 0;
+      BwdParams dummy = {};
+      const int st = launch_stream(ds, bp->kernel, dummy, pl, nullptr, "bwd_stream", true, &grid);
+      if (st == RMSNORM_B200_OK) {
+        bp->stream = true;
+        bp->pl = pl;
+        bp->grid = grid;
+        bp->nparts = static_cast<int64_t>(pl.nclusters) * pl.rps;
+        return RMSNORM_B200_OK;
+      }
+      if (st != RMSNORM_B200_ERR_UNSUPPORTED) return st;
+      why = "cluster not schedulable";
+    }
+  }
+  bp->stream = false;
+  bp->why = why;
+  const int64_t nsup = a->rows / a->heads;
+  const int64_t col_blocks = (bp->W + kGenericThreads - 1) / kGenericThreads;
+  int64_t target = std::max<int64_t>(1, (4 * ds->sm_count + col_blocks - 1) / col_blocks);
+  target = std::min<int64_t>(target, 1024);
+  bp->chunk_rows = std::max<int64_t>(1, (nsup + target - 1) / target);
+  bp->nparts = nsup > 0 ? (nsup + bp->chunk_rows - 1) / bp->chunk_rows : 0;
+  return RMSNORM_B200_OK;
+}
+
+size_t workspace_for(const BwdPlan& bp) {
+  const size_t per = static_cast<size_t>(bp.nparts) * static_cast<size_t>(bp.W) * sizeof(float);
+  return (bp.need_dw ? per : 0) + (bp.need_db ? per : 0);
+}
+
+int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  int st = check_bwd(a);
+  if (st) return st;
+  DeviceState* ds = nullptr;
+  st = get_device_state(&ds);
+  if (st) return st;
+  BwdPlan bp;
+  st = plan_bwd(ds, a, &bp);
+  if (st) return st;
+  const size_t need = workspace_for(bp);
+  if (need > ws_bytes || (need > 0 && (!ws || !aligned16(ws)))) return RMSNORM_B200_ERR_WORKSPACE;
+  float* dw_part = bp.need_dw ? static_cast<float*>(ws) : nullptr;
+  float* db_part = bp.need_db ? static_cast<float*>(ws) + (bp.need_dw ? bp.nparts * bp.W : 0) : nullptr;
+
+  if (a->rows > 0) {
+    if (bp.stream) {
+      BwdParams p = {};
+      p.x = a->x; p.dy = a->dout; p.dro = a->dresidual_out; p.rstd = a->rstd; p.w = a->weight;
+      p.dx = a->dx; p.dres = a->dresidual; p.dw_part = dw_part; p.db_part = db_part;
+      p.w_dt = a->weight_dtype; p.dro_dt = a->dresidual_out_dtype; p.dres_dt = a->dresidual_dtype;
+      p.w_per_head = a->weight && a->weight_heads > 1;
+      StreamPlan pl = bp.pl;
+      st = launch_stream(ds, bp.kernel, p, pl, stream, "bwd_stream", false, nullptr);
+      if (st) return st;
+    } else {
+      GenBwdParams g = {};
+      g.rows = a->rows; g.N = a->hidden; g.H = a->heads;
+      g.x = a->x; g.x_dt = a->x_dtype; g.dy = a->dout; g.dy_dt = a->dout_dtype;
+      g.rstd = a->rstd; g.w = a->weight; g.w_dt = a->weight_dtype;
+      g.w_ph = a->weight && a->weight_heads > 1;
+      g.dro = a->dresidual_out; g.dro_dt = a->dresidual_out_dtype;
+      g.dx = a->dx; g.dx_dt = a->dx_dtype; g.dres = a->dresidual; g.dres_dt = a->dresidual_dtype;
+      const int64_t grid = std::min<int64_t>(a->rows, static_cast<int64_t>(ds->sm_count) * 8);
+      bwd_generic_dx_kernel<<<static_cast<unsigned>(grid), kGenericThreads, 0, stream>>>(g);
+      if (cudaGetLastError() != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+      g_launches.fetch_add(1, std::memory_order_relaxed);
+      if ((dw_part || db_part) && bp.nparts > 0) {
+        dim3 pg(static_cast<unsigned>((bp.W + kGenericThreads - 1) / kGenericThreads),
+                static_cast<unsigned>(bp.nparts));
+        bwd_generic_partials_kernel<<<pg, kGenericThreads, 0, stream>>>(g, bp.chunk_rows, dw_part, db_part);
+        if (cudaGetLastError() != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+      }
+      t_last_plan = "bwd_generic (" + bp.why + ") grid=" + std::to_string(grid) +
+                    " chunks=" + std::to_string(bp.nparts);
+    }
+  } else {
+    t_last_plan = "bwd empty";
+  }
+
+  const int64_t nparts = a->rows > 0 ? bp.nparts : 0;
+  auto reduce = [&](const float* part, void* outp, int out_dt, int out_heads) -> int {
+    const int fold = (out_heads == 1 && a->heads > 1) ? a->heads : 1;
+    const int64_t wout = fold > 1 ? a->hidden : bp.W;
+    const unsigned blocks = static_cast<unsigned>((wout + kGenericThreads - 1) / kGenericThreads);
+    reduce_partials_kernel<<<blocks, kGenericThreads, 0, stream>>>(part, nparts, bp.W, a->hidden, fold,
+                                                                  outp, out_dt);
+    if (cudaGetLastError() != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return RMSNORM_B200_OK;
+  };
+  if (a->dweight) {
+    st = reduce(dw_part, a->dweight, a->dweight_dtype, a->weight_heads);
+    if (st) return st;
+  }
+  if (a->dbias) {
+    st = reduce(db_part, a->dbias, a->dbias_dtype, a->dbias_heads);
+    if (st) return st;
+  }
+  return RMSNORM_B200_OK;
+}
+
+}  // namespace
+}  // namespace rmsb200
+
+// =========================================================================================
+// C ABI
+// =========================================================================================
+using namespace rmsb200;
+
+extern "C" int rmsnorm_b200_fwd(const rmsnorm_b200_fwd_args* args, void* stream) {
+  return do_fwd(args, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int rmsnorm_b200_bwd_workspace_size(const rmsnorm_b200_bwd_args* args, size_t* bytes) {
+  if (!bytes) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  *bytes = 0;
+  int st = check_bwd(args);
+  if (st) return st;
+  DeviceState* ds = nullptr;
+  st = get_device_state(&ds);
+  if (st) return st;
+  BwdPlan bp;
+  st = plan_bwd(ds, args, &bp);
+  if (st) return st;
+  *bytes = workspace_for(bp);
+  return RMSNORM_B200_OK;
+}
+
+extern "C" int rmsnorm_b200_bwd(const rmsnorm_b200_bwd_args* args, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  return do_bwd(args, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" const char* rmsnorm_b200_strerror(int status) {
+  switch (status) {
+    case RMSNORM_B200_OK: return "ok";
+    case RMSNORM_B200_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case RMSNORM_B200_ERR_UNSUPPORTED: return "unsupported configuration";
+    case RMSNORM_B200_ERR_WORKSPACE: return "workspace missing, too small or misaligned";
+    case RMSNORM_B200_ERR_CUDA: return "CUDA launch or runtime error";
+    case RMSNORM_B200_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
+    case RMSNORM_B200_ERR_NO_DEVICE: return "no CUDA device";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int rmsnorm_b200_device_status(void* stream, int32_t* status, int32_t* where, int32_t clear) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = 0, wh = 0;
+  if (cudaMemcpyFromSymbolAsync(&st, g_status, sizeof(int), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaMemcpyFromSymbolAsync(&wh, g_status_where, sizeof(int), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return RMSNORM_B200_ERR_CUDA;
+  if (clear) {
+    static const int zero = 0;
+    if (cudaMemcpyToSymbolAsync(g_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyToSymbolAsync(g_status_where, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s) != cudaSuccess)
+      return RMSNORM_B200_ERR_CUDA;
+  }
+  if (cudaStreamSynchronize(s) != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+  if (status) *status = st;
+  if (where) *where = wh;
+  return RMSNORM_B200_OK;
+}
+
+extern "C" int rmsnorm_b200_set_wait_timeout_ns(uint64_t timeout_ns) {
+  unsigned long long v = timeout_ns;
+  if (cudaMemcpyToSymbol(g_wait_timeout_ns, &v, sizeof(v)) != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+  return RMSNORM_B200_OK;
+}
+
+extern "C" int rmsnorm_b200_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(timeout_ns);
+  if (cudaGetLastError() != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return RMSNORM_B200_OK;
+}
+
+extern "C" int rmsnorm_b200_abi_version(void) { return RMSNORM_B200_ABI_VERSION; }
+
+extern "C" uint64_t rmsnorm_b200_launch_count(void) { return g_launches.load(); }
+
+extern "C" int rmsnorm_b200_last_plan(char* buf, size_t len) {
+  const std::string& s = t_last_plan;
+  if (buf && len > 0) {
+    const size_t n = std::min(len - 1, s.size());
+    std::memcpy(buf, s.data(), n);
+    buf[n] = '\0';
+  }
+  return static_cast<int>(s.size());
+}

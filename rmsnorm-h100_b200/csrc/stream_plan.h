@@ -1,0 +1,74 @@
+// stream_plan.h -- launch plan shared by the host planner and the streaming kernels.
+#pragma once
+
+#include <cstdint>
+
+namespace rmsb200 {
+
+// Layout vocabulary used throughout the library:
+//   super-row : the H*N elements of one token; H = 1 for a shared affine. A super-row of
+//               a per-head tensor holds H rows of N elements (one per head).
+//   segment   : one normalisation row (N elements) inside a super-row.
+//   vector    : 8 consecutive elements (16 B for fp16/bf16, 32 B for fp32).
+//   slice     : the part of a super-row one CTA owns. Equal to the super-row unless the
+//               row is split across a thread-block cluster of P CTAs (P > 1).
+//   tile      : R consecutive super-rows staged into one shared-memory stage by TMA.
+//   sweep     : rps super-rows processed concurrently by rps thread groups of G threads.
+struct StreamPlan {
+  int32_t T;          // threads of the CTA (multiple of 32); thread 0 also issues the copies
+  int32_t G;          // consumer threads per super-row
+  int32_t rps;        // super-rows per sweep (T / G)
+  int32_t R;          // super-rows per tile (multiple of rps)
+  int32_t S;          // shared-memory stages
+  int32_t P;          // CTAs per cluster = slices per super-row
+  int32_t seg_mode;   // 1: segments of `vs` vectors reduced with xor shuffles; 0: whole slice
+  int32_t vs;         // segment length in vectors (seg_mode)
+  int32_t vslice;     // vectors per slice
+  int32_t heads;      // H
+  int32_t N;          // hidden size (segment length in elements)
+  int32_t nclusters;  // clusters in the grid (= CTAs when P == 1)
+  int64_t nrows;      // super-rows
+  int64_t ntiles;
+  int64_t W;          // super-row width in elements (H * N)
+  uint32_t stage_bytes;
+  uint32_t off[4];    // byte offsets within a stage: input 0, input 1, input 2, rstd
+  uint32_t row_bytes[3];  // bytes of one super-row slice of inputs 0..2 (0 = absent)
+};
+
+constexpr int kMaxVecs = 4;          // vectors per thread per super-row slice
+constexpr int kConsumerThreads = 512;
+constexpr int kBlockThreads = kConsumerThreads;  // 512 threads -> up to 128 registers
+constexpr int kMaxStages = 8;
+constexpr int kMaxCluster = 16;
+constexpr int kSmemReserve = 1024;   // barriers + reduction scratch after the stages
+
+struct FwdParams {
+  StreamPlan pl;
+  const void* x;
+  const void* res;
+  const void* w;
+  const void* b;
+  void* out;
+  void* ro;
+  float* rstd;
+  int32_t w_dt, b_dt, out_dt, ro_dt;
+  int32_t w_per_head, b_per_head;  // 1 when the affine tensor is [H, N]
+  float eps;
+};
+
+struct BwdParams {
+  StreamPlan pl;
+  const void* x;
+  const void* dy;
+  const void* dro;
+  const float* rstd;
+  const void* w;
+  void* dx;
+  void* dres;
+  float* dw_part;   // [nclusters][W] fp32 or null
+  float* db_part;   // [nclusters][W] fp32 or null
+  int32_t w_dt, dro_dt, dres_dt;
+  int32_t w_per_head;
+};
+
+}  // namespace rmsb200
