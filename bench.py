@@ -419,9 +419,15 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="time eager launches instead of a graph replay")
+    ap.add_argument("--rows", type=int, default=0, help="override the rows per rank (profiling runs)")
+    ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.rows:
+        w["rows"] = args.rows - args.rows % w.get("heads", 1)
+        w["desc"] += f" [rows overridden: {w['rows']}]"
 
     if args.impl == "reference":
         run_reference_arm(args, w)
@@ -452,37 +458,58 @@ def main():
     for i in range(args.warmup):
         runners[i % pool].step()
     torch.cuda.synchronize(dev)
+    # The K timed steps are captured once into a CUDA graph and replayed, so the device
+    # time is not diluted by Python/ctypes launch overhead (the library's launches are
+    # capturable: no allocation, no synchronisation). The multi-GPU backward keeps eager
+    # launches because its step contains the NCCL all-reduce.
+    use_graph = not (w["kind"] == "bwd" and group is not None) and not args.eager
+    graph = None
+    if use_graph:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        c0 = _lib.launch_count()
+        with torch.cuda.graph(graph, stream=side):
+            for i in range(args.steps):
+                runners[i % pool].step()
+        launches_per_graph = _lib.launch_count() - c0
+        stream.wait_stream(side)
+        graph.replay()  # one untimed replay on top of the eager warm-up steps
+        torch.cuda.synchronize(dev)
     barrier(group)
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     n_launch0 = _lib.launch_count()
     with ClockSampler(local) as clk:
         torch.cuda.synchronize(dev)
         t0.record(stream)
-        for i in range(args.steps):
-            starts[i].record(stream)
-            runners[i % pool].step()
-            ends[i].record(stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(args.steps):
+                runners[i % pool].step()
         t1.record(stream)
         torch.cuda.synchronize(dev)
-    launches = _lib.launch_count() - n_launch0
+    # launches inside the timed region: the graph replays exactly the captured launches
+    launches = (_lib.launch_count() - n_launch0) if graph is None else launches_per_graph
     barrier(group)
     total_ms = max_over_ranks(t0.elapsed_time(t1), dev, group)
     ms_step = total_ms / args.steps
-    kern_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    # one launch of the dominant kernel per step; in the backward the step also holds the
+    # small dweight/dbias reduction kernel(s) (and the all-reduce when N > 1), so the
+    # backward's achieved figure below is a lower bound for the streaming kernel alone
+    kern_ms = t0.elapsed_time(t1) / args.steps
     value = algo_bytes(w) * world / (ms_step * 1e-3) / 1e9
 
     peak, peak_kind = peaks()
-    # per-step events bracket the dominant kernel; in the backward they also hold the small
-    # dweight/dbias reduction kernel(s) (and the all-reduce when N > 1), so the backward's
-    # achieved figure is a lower bound for the streaming kernel alone
     achieved = main_kernel_bytes(w) / (kern_ms * 1e-3) / 1e9
 
-    e2e_ms, h2d, d2h = e2e_measure(w, sets[0], dev, max(1, args.e2e_steps), group)
-    e2e_value = algo_bytes(w) * world / (e2e_ms * 1e-3) / 1e9
+    if args.no_e2e:
+        e2e_ms, h2d, d2h, e2e_value = float("nan"), 0, 0, None
+    else:
+        e2e_ms, h2d, d2h = e2e_measure(w, sets[0], dev, max(1, args.e2e_steps), group)
+        e2e_value = algo_bytes(w) * world / (e2e_ms * 1e-3) / 1e9
 
     line = None
     if rank == 0:
@@ -501,6 +528,7 @@ def main():
                 "bytes_per_step_per_rank": algo_bytes(w),
                 "l2": ("inputs larger than L2" if pool == 1 else f"rotating pool of {pool} input sets > L2"),
                 "path": _lib.last_plan(),
+                "timing": "CUDA graph replay of the K steps" if graph is not None else "eager launches",
             },
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic_for(args.workload),
@@ -508,8 +536,9 @@ def main():
                          else "fallback 6.65 TB/s", "kernel_ms": round(kern_ms, 5),
                          "bytes_per_launch": main_kernel_bytes(w)},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
+            "e2e": None if e2e_value is None else {
+                "value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }

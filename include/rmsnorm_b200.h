@@ -24,7 +24,8 @@
  *                           <- no counterpart: the reference's mbarrier waits are unbounded
  *                              (ptx_rmsnorm_kernels.cu:957-986). Every wait here is bounded
  *                              and reports through a device status word.
- *   rmsnorm_b200_abi_version, rmsnorm_b200_launch_count, rmsnorm_b200_last_plan
+ *   rmsnorm_b200_abi_version, rmsnorm_b200_launch_count, rmsnorm_b200_last_plan,
+ *   rmsnorm_b200_max_active_clusters
  *                           <- no counterpart (introspection for tests and benchmarks).
  *
  * Semantics (identical to the reference's fp32 math, rmsnorm/rmsnorm.py:230-271, 390-399):
@@ -149,6 +150,11 @@ int rmsnorm_b200_set_wait_timeout_ns(uint64_t timeout_ns);
 int rmsnorm_b200_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
 
 int rmsnorm_b200_abi_version(void);
+
+/* How many clusters of `cluster_size` CTAs of the streaming kernels (512 threads, the full
+ * shared-memory carve-out) the current device can hold at once; 1 CTA per SM. Used by the
+ * planner to size grids; exported for tests and benchmarks. */
+int rmsnorm_b200_max_active_clusters(int32_t cluster_size, int32_t* clusters);
 
 /* Number of kernels this library has launched in this process (all devices). */
 uint64_t rmsnorm_b200_launch_count(void);

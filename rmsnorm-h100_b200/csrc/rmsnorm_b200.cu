@@ -322,8 +322,8 @@ int check_fwd(const rmsnorm_b200_fwd_args* a) {
   if (!a) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
   int st = check_common(a->rows, a->hidden, a->heads);
   if (st) return st;
-  if (!a->x || !a->out || !valid_dt(a->x_dtype) || !valid_dt(a->out_dtype))
-    return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (!valid_dt(a->x_dtype) || !valid_dt(a->out_dtype)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->rows > 0 && (!a->x || !a->out)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
   if (a->residual && !valid_dt(a->residual_dtype)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
   if (a->residual_out && !valid_dt(a->residual_out_dtype)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
   if (a->weight && (!valid_dt(a->weight_dtype) || (a->weight_heads != 1 && a->weight_heads != a->heads)))
@@ -342,7 +342,7 @@ int check_bwd(const rmsnorm_b200_bwd_args* a) {
   if (!a) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
   int st = check_common(a->rows, a->hidden, a->heads);
   if (st) return st;
-  if (!a->x || !a->dout || !a->rstd || !a->dx) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->rows > 0 && (!a->x || !a->dout || !a->rstd || !a->dx)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
   if (!valid_dt(a->x_dtype) || !valid_dt(a->dout_dtype) || !valid_dt(a->dx_dtype))
     return RMSNORM_B200_ERR_INVALID_ARGUMENT;
   if (a->weight && (!valid_dt(a->weight_dtype) || (a->weight_heads != 1 && a->weight_heads != a->heads)))
@@ -447,7 +447,6 @@ int plan_bwd(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdPlan* bp) {
     for (const void* p : ptrs)
       if (p && !aligned16(p)) { ok = false; why = "unaligned pointer"; }
   }
-  if (ok && a->dx_dtype != a->dout_dtype) { ok = false; why = "dx dtype != dout dtype"; }
   if (ok) {
     bp->kernel = pick_bwd(a->x_dtype, a->dout_dtype, bp->need_db);
     if (!bp->kernel) { ok = false; why = "dtype combination"; }
@@ -508,6 +507,7 @@ int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream
       p.x = a->x; p.dy = a->dout; p.dro = a->dresidual_out; p.rstd = a->rstd; p.w = a->weight;
       p.dx = a->dx; p.dres = a->dresidual; p.dw_part = dw_part; p.db_part = db_part;
       p.w_dt = a->weight_dtype; p.dro_dt = a->dresidual_out_dtype; p.dres_dt = a->dresidual_dtype;
+      p.dx_dt = a->dx_dtype;
       p.w_per_head = a->weight && a->weight_heads > 1;
       StreamPlan pl = bp.pl;
       st = launch_stream(ds, bp.kernel, p, pl, stream, "bwd_stream", false, nullptr);
@@ -633,6 +633,18 @@ extern "C" int rmsnorm_b200_selftest_wait_timeout(uint64_t timeout_ns, void* str
   selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(timeout_ns);
   if (cudaGetLastError() != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
   g_launches.fetch_add(1, std::memory_order_relaxed);
+  return RMSNORM_B200_OK;
+}
+
+extern "C" int rmsnorm_b200_max_active_clusters(int32_t cluster_size, int32_t* clusters) {
+  if (!clusters || cluster_size < 1 || cluster_size > kMaxCluster) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  DeviceState* ds = nullptr;
+  int st = get_device_state(&ds);
+  if (st) return st;
+  const void* k = reinterpret_cast<const void*>(fwd_stream_kernel<__nv_bfloat16, __nv_bfloat16>);
+  const int smem = 232448;
+  if (ensure_attrs(ds, k, smem)) return RMSNORM_B200_ERR_CUDA;
+  *clusters = resident_units(ds, k, cluster_size, smem);
   return RMSNORM_B200_OK;
 }
 

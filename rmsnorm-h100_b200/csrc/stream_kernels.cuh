@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) fwd_stream_kernel(const FwdP
     const int s = static_cast<int>(i % pl.S);
     const bool ok = mbar_wait(&L.full[s], static_cast<uint32_t>(i / pl.S) & 1u, kSiteFwdFull);
     if (__syncthreads_or(!ok || failed)) { failed = true; break; }
-    if (tid == 0 && i > 0) {  // everyone is past tile i-1: its stage is free
+    if (tid == 0 && i > 0 && pl.S > 1) {  // everyone is past tile i-1: its stage is free
       const int64_t t = cid + (i - 1 + pl.S) * ncl;
       if (t < pl.ntiles) { fwd_issue<X, RT>(p, pl, L, smem, t, static_cast<int>((i - 1) % pl.S), slice_elt0, pol); ++issued; }
     }
@@ -280,6 +280,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1) fwd_stream_kernel(const FwdP
           }
         }
       }
+    }
+    if (pl.S == 1) {  // a single stage is refilled once everyone is done with it
+      __syncthreads();
+      const int64_t t = cid + (i + 1) * ncl;
+      if (tid == 0 && t < pl.ntiles) { fwd_issue<X, RT>(p, pl, L, smem, t, 0, slice_elt0, pol); ++issued; }
     }
   }
   failed = __syncthreads_or(failed);
@@ -383,7 +388,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) bwd_stream_kernel(const BwdP
     const int s = static_cast<int>(i % pl.S);
     const bool ok = mbar_wait(&L.full[s], static_cast<uint32_t>(i / pl.S) & 1u, kSiteBwdFull);
     if (__syncthreads_or(!ok || failed)) { failed = true; break; }
-    if (tid == 0 && i > 0) {
+    if (tid == 0 && i > 0 && pl.S > 1) {
       const int64_t t = cid + (i - 1 + pl.S) * ncl;
       if (t < pl.ntiles) {
         bwd_issue<X, DY>(p, pl, L, smem, t, static_cast<int>((i - 1) % pl.S), slice_elt0, rstd_per_row, sdro, pol);
@@ -462,9 +467,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1) bwd_stream_kernel(const BwdP
             for (int e = 0; e < 8; ++e) g[e] += a[e];
           }
           const int64_t ge = g0 + static_cast<int64_t>(v) * 8;
-          Vec8<DY>::store(static_cast<DY*>(p.dx) + ge, g);
+          store8_rt(p.dx, p.dx_dt, ge, g);
           if (p.dres != nullptr) store8_rt(p.dres, p.dres_dt, ge, g);
         }
+      }
+    }
+    if (pl.S == 1) {
+      __syncthreads();
+      const int64_t t = cid + (i + 1) * ncl;
+      if (tid == 0 && t < pl.ntiles) {
+        bwd_issue<X, DY>(p, pl, L, smem, t, 0, slice_elt0, rstd_per_row, sdro, pol);
+        ++issued;
       }
     }
   }

@@ -67,7 +67,7 @@ struct BwdParams {
   void* dres;
   float* dw_part;   // [nclusters][W] fp32 or null
   float* db_part;   // [nclusters][W] fp32 or null
-  int32_t w_dt, dro_dt, dres_dt;
+  int32_t w_dt, dro_dt, dres_dt, dx_dt;
   int32_t w_per_head;
 };
 

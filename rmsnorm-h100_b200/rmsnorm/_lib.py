@@ -104,6 +104,7 @@ SIGNATURES = {
     "rmsnorm_b200_set_wait_timeout_ns": (ctypes.c_int, [ctypes.c_uint64]),
     "rmsnorm_b200_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_void_p]),
     "rmsnorm_b200_abi_version": (ctypes.c_int, []),
+    "rmsnorm_b200_max_active_clusters": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]),
     "rmsnorm_b200_launch_count": (ctypes.c_uint64, []),
     "rmsnorm_b200_last_plan": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_size_t]),
 }
@@ -302,6 +303,14 @@ def selftest_wait_timeout(device: torch.device, ns: int) -> None:
             load_library().rmsnorm_b200_selftest_wait_timeout(ns, _stream_handle(device)),
             "rmsnorm_b200_selftest_wait_timeout",
         )
+
+
+def max_active_clusters(device: torch.device, cluster_size: int) -> int:
+    n = ctypes.c_int32(0)
+    with torch.cuda.device(device):
+        _check(load_library().rmsnorm_b200_max_active_clusters(cluster_size, ctypes.byref(n)),
+               "rmsnorm_b200_max_active_clusters")
+    return int(n.value)
 
 
 def launch_count() -> int:
