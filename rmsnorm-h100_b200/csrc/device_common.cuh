@@ -114,14 +114,11 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 
-// Bounded wait: returns false (after recording the error) when the phase has not
-// completed within g_wait_timeout_ns, or as soon as another thread of any CTA has
+// Bounded wait, slow path: returns false (after recording the error) when the phase has
+// not completed within g_wait_timeout_ns, or as soon as another thread of any CTA has
 // recorded an error.
-template <bool kClusterScope = false>
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int where) {
-  if (kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) {
-    return true;
-  }
+template <bool kClusterScope>
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int where) {
   const uint64_t t0 = globaltimer_ns();
   const uint64_t limit = g_wait_timeout_ns;
   uint32_t spins = 0;
@@ -137,6 +134,13 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int where
       }
     }
   }
+}
+
+// Bounded wait: one inline probe, then the out-of-line bounded loop.
+template <bool kClusterScope = false>
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int where) {
+  if (kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow<kClusterScope>(bar, parity, where);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -329,6 +333,17 @@ struct Vec8<__half> {
     u.w = pack_f16x2(v[6], v[7]);
     __stcs(reinterpret_cast<uint4*>(p), u);
   }
+};
+
+// Tag type for a tensor that is absent from a kernel instantiation.
+struct NoT {};
+template <typename T>
+struct Present {
+  static constexpr bool value = true;
+};
+template <>
+struct Present<NoT> {
+  static constexpr bool value = false;
 };
 
 // Runtime-dtype variants for tensors whose dtype is not a template parameter (outputs

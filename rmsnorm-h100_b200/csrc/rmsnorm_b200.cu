@@ -3,7 +3,7 @@
 // Dispatch (replaces launch_fwd / launch_bwd of the reference,
 // rmsnorm/csrc/ptx_rmsnorm_kernels.cu:4941-6600, and its per-(dtype, N) thread tables):
 //   * streaming kernels (stream_kernels.cuh) for every shape whose rows are 8-element
-//     vectorisable and 16-byte aligned, in the specialised dtype set;
+//     vectorisable and 16-byte aligned, in the specialised dtype combinations;
 //   * generic kernels (generic_kernels.cuh) for everything else;
 //   * backward dweight/dbias: per-(CTA, row group) fp32 partial rows written by the main
 //     kernel, summed in a fixed order by reduce_partials_kernel (deterministic; the
@@ -24,13 +24,24 @@
 #include "stream_kernels.cuh"
 
 namespace rmsb200 {
-
 namespace {
 
 std::atomic<uint64_t> g_launches{0};
 thread_local std::string t_last_plan;
 
-constexpr int kSmemBudget = 232448 - kSmemReserve;  // 227 KB opt-in minus barrier area
+// Shared memory an SM offers (228 KB), the opt-in maximum per CTA (227 KB), and the
+// 1 KB the runtime reserves per resident CTA.
+constexpr int kSmemPerSm = 233472;
+constexpr int kSmemOptIn = 232448;
+constexpr int kSmemSysReserve = 1024;
+
+struct BlockCfg {
+  int threads;
+  int ctas_per_sm;
+  int smem_budget;  // bytes of stages one CTA may use (barrier area excluded)
+};
+constexpr BlockCfg kLarge = {kBlockLarge, 1, kSmemOptIn - kSmemReserve};
+constexpr BlockCfg kSmall = {kBlockSmall, 2, kSmemPerSm / 2 - kSmemSysReserve - kSmemReserve};
 
 int elem_bytes(int dt) { return dt == RMSNORM_B200_F32 ? 4 : 2; }
 bool valid_dt(int dt) { return dt == RMSNORM_B200_F16 || dt == RMSNORM_B200_BF16 || dt == RMSNORM_B200_F32; }
@@ -46,7 +57,7 @@ struct DeviceState {
   int sm_count = 0;
   std::mutex mu;
   std::map<const void*, bool> attrs_done;
-  std::map<std::tuple<const void*, int, int>, int> occupancy;  // (kernel, P, smem) -> clusters or blocks/SM
+  std::map<std::tuple<const void*, int, int, int>, int> occupancy;  // (kernel, P, smem, threads)
 };
 
 std::mutex g_devices_mu;
@@ -67,33 +78,33 @@ int get_device_state(DeviceState** out) {
   return RMSNORM_B200_OK;
 }
 
-int ensure_attrs(DeviceState* ds, const void* kernel, int smem) {
+int ensure_attrs(DeviceState* ds, const void* kernel) {
   std::lock_guard<std::mutex> lock(ds->mu);
   if (ds->attrs_done.count(kernel)) return RMSNORM_B200_OK;
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448) != cudaSuccess)
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemOptIn) != cudaSuccess)
     return RMSNORM_B200_ERR_CUDA;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
     return RMSNORM_B200_ERR_CUDA;
-  (void)smem;
   ds->attrs_done[kernel] = true;
   return RMSNORM_B200_OK;
 }
 
-// Clusters of P CTAs (P > 1) or CTAs per SM (P == 1) that can be resident at once.
-int resident_units(DeviceState* ds, const void* kernel, int P, int smem) {
+// Clusters of P CTAs (P > 1) or CTAs (P == 1) that can be resident at once.
+int resident_units(DeviceState* ds, const void* kernel, int P, int smem, int threads) {
+  const auto key = std::make_tuple(kernel, P, smem, threads);
   {
     std::lock_guard<std::mutex> lock(ds->mu);
-    auto it = ds->occupancy.find(std::make_tuple(kernel, P, smem));
+    auto it = ds->occupancy.find(key);
     if (it != ds->occupancy.end()) return it->second;
   }
   int n = 0;
   if (P == 1) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kBlockThreads, smem) != cudaSuccess) n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess) n = 0;
     n *= ds->sm_count;
   } else {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(P * ds->sm_count);
-    cfg.blockDim = dim3(kBlockThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -106,7 +117,7 @@ int resident_units(DeviceState* ds, const void* kernel, int P, int smem) {
   }
   cudaGetLastError();  // a refused query must not poison the caller's next check
   std::lock_guard<std::mutex> lock(ds->mu);
-  ds->occupancy[std::make_tuple(kernel, P, smem)] = n;
+  ds->occupancy[key] = n;
   return n;
 }
 
@@ -121,23 +132,31 @@ int pow2_ceil(int v) {
   return p;
 }
 
+int log2i(int v) {
+  int s = 0;
+  while ((1 << s) < v) ++s;
+  return s;
+}
+
 bool is_pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
 
 uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-// Builds the thread/tile/stage/cluster plan for a streaming kernel. `in_bytes[k]` is the
-// element size of staged input k (0 = absent); `rstd_staged` adds the per-row rstd block
-// (backward). Returns false (with a reason) when the shape is outside what the streaming
-// kernels take.
+// Builds the thread/tile/stage/cluster plan for a streaming kernel launched with block
+// shape `bc`. `in_bytes[k]` is the element size of staged input k (0 = absent);
+// `rstd_staged` adds the per-row rstd block (backward); `max_vecs` is the kernel's vectors
+// per thread. `force_p` (0 = free) pins the cluster size. Returns false (with a reason)
+// when the shape is outside what the streaming kernels take.
 bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], bool rstd_staged,
-                      int max_vecs, StreamPlan* out, std::string* why) {
+                      int max_vecs, const BlockCfg& bc, int force_p, StreamPlan* out, std::string* why) {
   StreamPlan pl = {};
   if (N64 % 8 != 0 || N64 > (int64_t(1) << 30)) { *why = "hidden % 8 != 0"; return false; }
   const int N = static_cast<int>(N64);
   const int64_t W = static_cast<int64_t>(H) * N;
   if (W / 8 > (int64_t(1) << 24)) { *why = "row too long"; return false; }
   const int vrow = static_cast<int>(W / 8);
-  const int T = kConsumerThreads;
+  const int T = bc.threads;
+  const int budget = bc.smem_budget;
   pl.T = T;
   pl.heads = H;
   pl.N = N;
@@ -161,11 +180,10 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
     pl.vslice = vrow;
   } else {
     pl.seg_mode = 0;
-    pl.vs = 0;
+    pl.vs = 1;
     int bytes_per_vec = 0;
     for (int k = 0; k < 3; ++k) bytes_per_vec += 8 * in_bytes[k];
     const int max_p = std::min(kMaxCluster, env_int("RMSNORM_B200_MAX_CLUSTER", kMaxCluster));
-    const int force_p = env_int("RMSNORM_B200_FORCE_CLUSTER", 0);
     P = 0;
     for (int cand = 1; cand <= max_p; cand <<= 1) {
       if (force_p && cand != force_p) continue;
@@ -173,10 +191,10 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
       const int vs_ = vrow / cand;
       if (vs_ > T * max_vecs) continue;
       const int64_t slice_bytes = static_cast<int64_t>(vs_) * bytes_per_vec + (rstd_staged ? 16 : 0);
-      if (slice_bytes > kSmemBudget) continue;
+      if (slice_bytes > budget) continue;
       // prefer a split that leaves room for at least two stages
-      if (slice_bytes * 2 > kSmemBudget && cand < max_p && !force_p &&
-          vrow % (cand * 2) == 0 && (vrow / (cand * 2)) >= 32)
+      if (slice_bytes * 2 > budget && cand < max_p && !force_p && vrow % (cand * 2) == 0 &&
+          (vrow / (cand * 2)) >= 32)
         continue;
       P = cand;
       break;
@@ -186,6 +204,7 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
     const int per_thread_min = (pl.vslice + max_vecs - 1) / max_vecs;
     pl.G = std::min(T, static_cast<int>(align_up(static_cast<uint32_t>(per_thread_min), 32u)));
   }
+  pl.vs_shift = log2i(pl.vs);
   pl.P = P;
   pl.rps = P > 1 ? 1 : T / pl.G;
   if (pl.rps < 1) { *why = "group wider than the CTA"; return false; }
@@ -197,7 +216,7 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
   }
   const int rstd_per_row = pl.seg_mode ? H : 1;
   if (rstd_staged) per_row += 4u * rstd_per_row;
-  const int target = env_int("RMSNORM_B200_STAGE_BYTES", 48 * 1024);
+  const int target = env_int("RMSNORM_B200_STAGE_BYTES", 48 * 1024) * T / kBlockLarge;
   int R = pl.rps;
   if (P == 1) {
     const int64_t m = std::max<int64_t>(1, target / (static_cast<int64_t>(pl.rps) * per_row));
@@ -216,15 +235,15 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
     return off;
   };
   uint32_t stage = layout(R);
-  while (stage > static_cast<uint32_t>(kSmemBudget) && R > pl.rps) {
+  while (stage > static_cast<uint32_t>(budget) && R > pl.rps) {
     R -= pl.rps;
     stage = layout(R);
   }
-  if (stage > static_cast<uint32_t>(kSmemBudget)) { *why = "stage does not fit shared memory"; return false; }
+  if (stage > static_cast<uint32_t>(budget)) { *why = "stage does not fit shared memory"; return false; }
   pl.R = R;
   pl.stage_bytes = stage;
   const int max_s = std::max(1, std::min(kMaxStages, env_int("RMSNORM_B200_MAX_STAGES", kMaxStages)));
-  pl.S = std::max(1, std::min<int>(max_s, kSmemBudget / stage));
+  pl.S = std::max(1, std::min<int>(max_s, budget / static_cast<int>(stage)));
   pl.ntiles = (pl.nrows + R - 1) / R;
   *out = pl;
   return true;
@@ -242,15 +261,16 @@ std::string describe(const char* kind, const StreamPlan& pl, int grid) {
   return buf;
 }
 
+// Sizes the grid (persistent: as many clusters as can be resident, at most one per tile)
+// and, unless dry_run, launches. Returns UNSUPPORTED when no cluster of this shape fits.
 template <typename Params>
 int launch_stream(DeviceState* ds, void (*kernel)(const Params), Params params, StreamPlan& pl,
                   cudaStream_t stream, const char* kind, bool dry_run, int* grid_out) {
   const int smem = smem_bytes(pl);
-  if (ensure_attrs(ds, reinterpret_cast<const void*>(kernel), smem) != RMSNORM_B200_OK)
-    return RMSNORM_B200_ERR_CUDA;
-  const int units = resident_units(ds, reinterpret_cast<const void*>(kernel), pl.P, smem);
+  if (ensure_attrs(ds, reinterpret_cast<const void*>(kernel)) != RMSNORM_B200_OK) return RMSNORM_B200_ERR_CUDA;
+  const int units = resident_units(ds, reinterpret_cast<const void*>(kernel), pl.P, smem, pl.T);
   if (units <= 0) return RMSNORM_B200_ERR_UNSUPPORTED;
-  const int64_t nclusters = std::min<int64_t>(pl.ntiles, units);
+  const int64_t nclusters = std::min<int64_t>(std::max<int64_t>(pl.ntiles, 1), units);
   pl.nclusters = static_cast<int>(nclusters);
   const int grid = static_cast<int>(nclusters * pl.P);
   if (grid_out) *grid_out = grid;
@@ -258,7 +278,7 @@ int launch_stream(DeviceState* ds, void (*kernel)(const Params), Params params, 
   params.pl = pl;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kBlockThreads);
+  cfg.blockDim = dim3(pl.T);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -276,18 +296,30 @@ int launch_stream(DeviceState* ds, void (*kernel)(const Params), Params params, 
 }
 
 // ---------------------------------------------------------------------------------------
-// Kernel tables
+// Kernel tables: the specialised dtype combinations (absent tensor = -1 / NoT)
 // ---------------------------------------------------------------------------------------
 using FwdKernel = void (*)(const FwdParams);
 using BwdKernel = void (*)(const BwdParams);
+using h16 = __half;
+using b16 = __nv_bfloat16;
+constexpr int H = RMSNORM_B200_F16, B = RMSNORM_B200_BF16, F = RMSNORM_B200_F32, NA = -1;
 
-FwdKernel pick_fwd(int x_dt, int r_dt) {
-  // r_dt: dtype of the residual (equal to x_dt when there is none)
-  if (x_dt == RMSNORM_B200_BF16 && r_dt == RMSNORM_B200_BF16) return fwd_stream_kernel<__nv_bfloat16, __nv_bfloat16>;
-  if (x_dt == RMSNORM_B200_F16 && r_dt == RMSNORM_B200_F16) return fwd_stream_kernel<__half, __half>;
-  if (x_dt == RMSNORM_B200_F32 && r_dt == RMSNORM_B200_F32) return fwd_stream_kernel<float, float>;
-  if (x_dt == RMSNORM_B200_BF16 && r_dt == RMSNORM_B200_F32) return fwd_stream_kernel<__nv_bfloat16, float>;
-  if (x_dt == RMSNORM_B200_F16 && r_dt == RMSNORM_B200_F32) return fwd_stream_kernel<__half, float>;
+// (x, residual, out, residual_out)
+FwdKernel pick_fwd(int x, int r, int o, int ro) {
+#define RMSB_FWD(XT, XC, RT, RC, OT, OC, ROT, ROC)                              \
+  if (x == XC && r == RC && o == OC && ro == ROC)                               \
+    return fwd_stream_kernel<XT, RT, OT, ROT, kMaxVecs, kBlockLarge, 1>;
+  RMSB_FWD(b16, B, NoT, NA, b16, B, NoT, NA)
+  RMSB_FWD(h16, H, NoT, NA, h16, H, NoT, NA)
+  RMSB_FWD(float, F, NoT, NA, float, F, NoT, NA)
+  RMSB_FWD(b16, B, b16, B, b16, B, b16, B)
+  RMSB_FWD(h16, H, h16, H, h16, H, h16, H)
+  RMSB_FWD(float, F, float, F, float, F, float, F)
+  RMSB_FWD(b16, B, b16, B, b16, B, float, F)
+  RMSB_FWD(h16, H, h16, H, h16, H, float, F)
+  RMSB_FWD(b16, B, float, F, b16, B, float, F)
+  RMSB_FWD(h16, H, float, F, h16, H, float, F)
+#undef RMSB_FWD
   return nullptr;
 }
 
@@ -296,16 +328,39 @@ FwdKernel pick_fwd(int x_dt, int r_dt) {
 constexpr int kBwdVecsDb = 2;
 int bwd_max_vecs(bool has_db) { return has_db ? kBwdVecsDb : kMaxVecs; }
 
-BwdKernel pick_bwd(int x_dt, int dy_dt, bool has_db) {
-#define RMSB_BWD(XT, DT, XC, DC)                                                          \
-  if (x_dt == XC && dy_dt == DC)                                                          \
-    return has_db ? bwd_stream_kernel<XT, DT, true, kBwdVecsDb> : bwd_stream_kernel<XT, DT, false, kMaxVecs>;
-  RMSB_BWD(__nv_bfloat16, __nv_bfloat16, RMSNORM_B200_BF16, RMSNORM_B200_BF16)
-  RMSB_BWD(__half, __half, RMSNORM_B200_F16, RMSNORM_B200_F16)
-  RMSB_BWD(float, float, RMSNORM_B200_F32, RMSNORM_B200_F32)
-  RMSB_BWD(float, __nv_bfloat16, RMSNORM_B200_F32, RMSNORM_B200_BF16)
-  RMSB_BWD(float, __half, RMSNORM_B200_F32, RMSNORM_B200_F16)
+// (x, dout, dx, dresidual_out, dresidual), dbias, launch shape
+BwdKernel pick_bwd(int x, int dy, int dx, int dro, int dres, bool db, bool small) {
+#define RMSB_BWD_SHAPE(XT, XC, DT, DC, DXT, DXC, AT, AC, ST, SC, BLK, MINB)                       \
+  if (x == XC && dy == DC && dx == DXC && dro == AC && dres == SC)                                 \
+    return db ? bwd_stream_kernel<XT, DT, DXT, AT, ST, true, kBwdVecsDb, BLK, MINB>                \
+              : bwd_stream_kernel<XT, DT, DXT, AT, ST, false, kMaxVecs, BLK, MINB>;
+  if (small) {
+#define RMSB_BWD(...) RMSB_BWD_SHAPE(__VA_ARGS__, kBlockSmall, 2)
+    RMSB_BWD(b16, B, b16, B, b16, B, NoT, NA, NoT, NA)
+    RMSB_BWD(h16, H, h16, H, h16, H, NoT, NA, NoT, NA)
+    RMSB_BWD(float, F, float, F, float, F, NoT, NA, NoT, NA)
+    RMSB_BWD(float, F, b16, B, b16, B, NoT, NA, NoT, NA)
+    RMSB_BWD(float, F, h16, H, h16, H, NoT, NA, NoT, NA)
 #undef RMSB_BWD
+    return nullptr;
+  }
+#define RMSB_BWD(...) RMSB_BWD_SHAPE(__VA_ARGS__, kBlockLarge, 1)
+  RMSB_BWD(b16, B, b16, B, b16, B, NoT, NA, NoT, NA)
+  RMSB_BWD(h16, H, h16, H, h16, H, NoT, NA, NoT, NA)
+  RMSB_BWD(float, F, float, F, float, F, NoT, NA, NoT, NA)
+  RMSB_BWD(b16, B, b16, B, b16, B, b16, B, b16, B)
+  RMSB_BWD(h16, H, h16, H, h16, H, h16, H, h16, H)
+  RMSB_BWD(float, F, float, F, float, F, float, F, float, F)
+  RMSB_BWD(float, F, b16, B, b16, B, NoT, NA, NoT, NA)
+  RMSB_BWD(float, F, h16, H, h16, H, NoT, NA, NoT, NA)
+  RMSB_BWD(float, F, b16, B, b16, B, float, F, b16, B)
+  RMSB_BWD(float, F, h16, H, h16, H, float, F, h16, H)
+  RMSB_BWD(float, F, b16, B, b16, B, NoT, NA, float, F)
+  RMSB_BWD(float, F, h16, H, h16, H, NoT, NA, float, F)
+  RMSB_BWD(float, F, b16, B, b16, B, float, F, float, F)
+  RMSB_BWD(float, F, h16, H, h16, H, float, F, float, F)
+#undef RMSB_BWD
+#undef RMSB_BWD_SHAPE
   return nullptr;
 }
 
@@ -358,16 +413,6 @@ int check_bwd(const rmsnorm_b200_bwd_args* a) {
 // ---------------------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------------------
-bool fwd_stream_eligible(const rmsnorm_b200_fwd_args* a, std::string* why) {
-  if (a->hidden % 8) { *why = "hidden % 8"; return false; }
-  const void* ptrs[] = {a->x, a->residual, a->weight, a->bias, a->out, a->residual_out};
-  for (const void* p : ptrs)
-    if (p && !aligned16(p)) { *why = "unaligned pointer"; return false; }
-  const int r_dt = a->residual ? a->residual_dtype : a->x_dtype;
-  if (!pick_fwd(a->x_dtype, r_dt)) { *why = "dtype combination"; return false; }
-  return true;
-}
-
 int launch_fwd_generic(DeviceState* ds, const rmsnorm_b200_fwd_args* a, cudaStream_t stream,
                        const std::string& why) {
   GenFwdParams g = {};
@@ -395,26 +440,37 @@ int do_fwd(const rmsnorm_b200_fwd_args* a, cudaStream_t stream) {
   st = get_device_state(&ds);
   if (st) return st;
   std::string why;
-  const bool force_generic = env_int("RMSNORM_B200_FORCE_GENERIC", 0) != 0;
-  if (!force_generic && fwd_stream_eligible(a, &why)) {
+  FwdKernel kernel = nullptr;
+  if (env_int("RMSNORM_B200_FORCE_GENERIC", 0)) {
+    why = "forced";
+  } else if (a->hidden % 8) {
+    why = "hidden % 8";
+  } else {
+    const void* ptrs[] = {a->x, a->residual, a->weight, a->bias, a->out, a->residual_out};
+    for (const void* p : ptrs)
+      if (p && !aligned16(p)) why = "unaligned pointer";
+    if (why.empty()) {
+      kernel = pick_fwd(a->x_dtype, a->residual ? a->residual_dtype : NA, a->out_dtype,
+                        a->residual_out ? a->residual_out_dtype : NA);
+      if (!kernel) why = "dtype combination";
+    }
+  }
+  if (kernel) {
     StreamPlan pl;
-    const int r_dt = a->residual ? a->residual_dtype : a->x_dtype;
-    const int in_bytes[3] = {elem_bytes(a->x_dtype), a->residual ? elem_bytes(r_dt) : 0, 0};
-    if (make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, false, kMaxVecs, &pl, &why)) {
+    const int in_bytes[3] = {elem_bytes(a->x_dtype), a->residual ? elem_bytes(a->residual_dtype) : 0, 0};
+    if (make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, false, kMaxVecs, kLarge,
+                         env_int("RMSNORM_B200_FORCE_CLUSTER", 0), &pl, &why)) {
       FwdParams p = {};
       p.x = a->x; p.res = a->residual; p.w = a->weight; p.b = a->bias;
       p.out = a->out; p.ro = a->residual_out; p.rstd = a->rstd;
-      p.w_dt = a->weight_dtype; p.b_dt = a->bias_dtype; p.out_dt = a->out_dtype;
-      p.ro_dt = a->residual_out_dtype;
+      p.w_dt = a->weight_dtype; p.b_dt = a->bias_dtype;
       p.w_per_head = a->weight && a->weight_heads > 1;
       p.b_per_head = a->bias && a->bias_heads > 1;
       p.eps = a->eps;
-      st = launch_stream(ds, pick_fwd(a->x_dtype, r_dt), p, pl, stream, "fwd_stream", false, nullptr);
+      st = launch_stream(ds, kernel, p, pl, stream, "fwd_stream", false, nullptr);
       if (st != RMSNORM_B200_ERR_UNSUPPORTED) return st;
       why = "cluster not schedulable";
     }
-  } else if (force_generic) {
-    why = "forced";
   }
   return launch_fwd_generic(ds, a, stream, why);
 }
@@ -434,6 +490,30 @@ struct BwdPlan {
   std::string why;
 };
 
+// Tries one (block shape, kernel) candidate; on success fills bp and returns true.
+bool try_bwd_stream(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdKernel kernel, const BlockCfg& bc,
+                    int force_p, BwdPlan* bp, std::string* why) {
+  if (!kernel) return false;
+  const int in_bytes[3] = {elem_bytes(a->x_dtype), elem_bytes(a->dout_dtype),
+                           a->dresidual_out ? elem_bytes(a->dresidual_out_dtype) : 0};
+  StreamPlan pl;
+  if (!make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, true, bwd_max_vecs(bp->need_db), bc, force_p,
+                        &pl, why))
+    return false;
+  int grid = 0;
+  BwdParams dummy = {};
+  if (launch_stream(ds, kernel, dummy, pl, nullptr, "bwd_stream", true, &grid) != RMSNORM_B200_OK) {
+    *why = "cluster not schedulable";
+    return false;
+  }
+  bp->stream = true;
+  bp->kernel = kernel;
+  bp->pl = pl;
+  bp->grid = grid;
+  bp->nparts = static_cast<int64_t>(pl.nclusters) * pl.rps;
+  return true;
+}
+
 int plan_bwd(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdPlan* bp) {
   bp->W = a->hidden * a->heads;
   bp->need_dw = a->dweight != nullptr;
@@ -448,28 +528,30 @@ int plan_bwd(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdPlan* bp) {
       if (p && !aligned16(p)) { ok = false; why = "unaligned pointer"; }
   }
   if (ok) {
-    bp->kernel = pick_bwd(a->x_dtype, a->dout_dtype, bp->need_db);
-    if (!bp->kernel) { ok = false; why = "dtype combination"; }
-  }
-  if (ok) {
-    const int in_bytes[3] = {elem_bytes(a->x_dtype), elem_bytes(a->dout_dtype),
-                             a->dresidual_out ? elem_bytes(a->dresidual_out_dtype) : 0};
-    StreamPlan pl;
-    if (make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, true, bwd_max_vecs(bp->need_db), &pl,
-                         &why)) {
-      int grid = 0;
-      BwdParams dummy = {};
-      const int st = launch_stream(ds, bp->kernel, dummy, pl, nullptr, "bwd_stream", true, &grid);
-      if (st == RMSNORM_B200_OK) {
-        bp->stream = true;
-        bp->pl = pl;
-        bp->grid = grid;
-        bp->nparts = static_cast<int64_t>(pl.nclusters) * pl.rps;
-        return RMSNORM_B200_OK;
-      }
-      if (st != RMSNORM_B200_ERR_UNSUPPORTED) return st;
-      why = "cluster not schedulable";
+    const int dro = a->dresidual_out ? a->dresidual_out_dtype : NA;
+    const int dres = a->dresidual ? a->dresidual_dtype : NA;
+    BwdKernel large = pick_bwd(a->x_dtype, a->dout_dtype, a->dx_dtype, dro, dres, bp->need_db, false);
+    BwdKernel small = pick_bwd(a->x_dtype, a->dout_dtype, a->dx_dtype, dro, dres, bp->need_db, true);
+    const int force_p = env_int("RMSNORM_B200_FORCE_CLUSTER", 0);
+    const int shape = env_int("RMSNORM_B200_BWD_SHAPE", 0);  // 0 auto, 1 large only, 2 small only
+    if (!large && !small) why = "dtype combination";
+    // A row split across a cluster waits once per row for its peers. With two CTAs of
+    // 256 threads per SM, two such row pipelines overlap on every SM; prefer that shape
+    // when the cluster split it needs keeps at least as many SMs busy.
+    BwdPlan cand_large = *bp, cand_small = *bp;
+    std::string why_l, why_s;
+    const bool have_large = shape != 2 && try_bwd_stream(ds, a, large, kLarge, force_p, &cand_large, &why_l);
+    bool have_small = false;
+    if (shape != 1 && small && (!have_large || cand_large.pl.P > 1 || shape == 2))
+      have_small = try_bwd_stream(ds, a, small, kSmall, force_p, &cand_small, &why_s);
+    if (have_small && have_large) {
+      const int64_t sms_large = static_cast<int64_t>(cand_large.grid);
+      const int64_t sms_small = static_cast<int64_t>(cand_small.grid) / kSmall.ctas_per_sm;
+      if (sms_small < sms_large) have_small = false;
     }
+    if (have_small) { *bp = cand_small; return RMSNORM_B200_OK; }
+    if (have_large) { *bp = cand_large; return RMSNORM_B200_OK; }
+    if (why.empty()) why = why_l.empty() ? why_s : why_l;
   }
   bp->stream = false;
   bp->why = why;
@@ -506,8 +588,7 @@ int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream
       BwdParams p = {};
       p.x = a->x; p.dy = a->dout; p.dro = a->dresidual_out; p.rstd = a->rstd; p.w = a->weight;
       p.dx = a->dx; p.dres = a->dresidual; p.dw_part = dw_part; p.db_part = db_part;
-      p.w_dt = a->weight_dtype; p.dro_dt = a->dresidual_out_dtype; p.dres_dt = a->dresidual_dtype;
-      p.dx_dt = a->dx_dtype;
+      p.w_dt = a->weight_dtype;
       p.w_per_head = a->weight && a->weight_heads > 1;
       StreamPlan pl = bp.pl;
       st = launch_stream(ds, bp.kernel, p, pl, stream, "bwd_stream", false, nullptr);
@@ -641,10 +722,9 @@ extern "C" int rmsnorm_b200_max_active_clusters(int32_t cluster_size, int32_t* c
   DeviceState* ds = nullptr;
   int st = get_device_state(&ds);
   if (st) return st;
-  const void* k = reinterpret_cast<const void*>(fwd_stream_kernel<__nv_bfloat16, __nv_bfloat16>);
-  const int smem = 232448;
-  if (ensure_attrs(ds, k, smem)) return RMSNORM_B200_ERR_CUDA;
-  *clusters = resident_units(ds, k, cluster_size, smem);
+  const void* k = reinterpret_cast<const void*>(pick_fwd(B, NA, B, NA));
+  if (ensure_attrs(ds, k)) return RMSNORM_B200_ERR_CUDA;
+  *clusters = resident_units(ds, k, cluster_size, kSmemOptIn, kBlockLarge);
   return RMSNORM_B200_OK;
 }
 

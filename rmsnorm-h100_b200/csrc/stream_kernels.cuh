@@ -1,37 +1,45 @@
 // stream_kernels.cuh -- the persistent, TMA-staged forward and backward kernels.
 //
 // Structure (both directions):
-//   * one CTA of T = 512 threads per SM (or one cluster of P CTAs on P SMs), persistent
-//     over tiles assigned round-robin (tile = cluster id + k * clusters);
+//   * one CTA of 512 threads per SM, or two CTAs of 256 threads per SM (launch variant for
+//     rows split across clusters, so that two independent row pipelines share each SM);
+//     persistent over tiles assigned round-robin (tile = cluster id + k * clusters);
 //   * thread 0 streams each tile HBM -> shared memory with cp.async.bulk (one bulk copy
 //     per tensor per tile when P == 1, one per row slice when P > 1) into an S-deep ring of
 //     stages; each stage's "full" mbarrier counts the bytes landing. Right after the
-//     CTA-wide barrier that opens tile i, thread 0 refills the stage tile i-1 used with
-//     tile i-1+S, so S-1 tiles are always in flight behind the one being computed;
+//     CTA-wide vote that opens tile i, thread 0 refills the stage tile i-1 used with tile
+//     i-1+S, so S-1 tiles are always in flight behind the one being computed;
 //   * threads read 8-element vectors from shared memory, reduce the row (xor shuffles in a
-//     warp, named barriers across the warps of a row group, st.async + mbarrier exchange
-//     through distributed shared memory across the CTAs of a cluster), then re-read the
-//     stage and write outputs with 16-byte coalesced streaming stores;
+//     warp, one named barrier + one shared load + a second shuffle tree across the warps of
+//     a row group, st.async + mbarrier exchange through distributed shared memory across
+//     the CTAs of a cluster), then re-read the stage and write outputs with 16-byte
+//     coalesced streaming stores;
+//   * every per-element dtype is a template parameter (absent tensors are `NoT`), so the
+//     inner loops carry no runtime type dispatch;
 //   * affine parameters live in registers for the whole kernel (each thread always owns
 //     the same columns), so dweight/dbias accumulate in registers and are written once
-//     per (CTA, row group) as a partial row; a second kernel sums the partials in a fixed
-//     order.
+//     per (cluster, row group) as a partial row; a second kernel sums the partials in a
+//     fixed order.
 // Every wait is bounded; a wait that gives up records an error in the device status word
 // and the CTA leaves its loop at the next CTA-wide vote (after its in-flight copies land).
 #pragma once
+
+#include <type_traits>
 
 #include "device_common.cuh"
 #include "stream_plan.h"
 
 namespace rmsb200 {
 
+constexpr int kXSlots = 4;  // cluster exchange slots (sequence number mod 4)
+
 struct SmemLayout {
   uint64_t* full;   // [kMaxStages]
-  uint64_t* xbar;   // [2] cluster exchange barriers
-  float* xpart;     // [2][kMaxCluster] partial sums received from the cluster
+  uint64_t* xbar;   // [kXSlots] cluster exchange barriers
+  float* xpart;     // [kXSlots][kMaxCluster] partial sums received from the cluster
   float* red;       // [2][32] per-warp partials (double buffered)
-  float* bc;        // [2] cluster total broadcast to the row group
-  int* bcf;         // [2] ... and whether the exchange completed
+  float* bc;        // [kXSlots] cluster total broadcast to the row group
+  int* bcf;         // [kXSlots] ... and whether the exchange completed
 };
 
 __device__ __forceinline__ SmemLayout carve_smem(unsigned char* smem, const StreamPlan& pl) {
@@ -39,65 +47,68 @@ __device__ __forceinline__ SmemLayout carve_smem(unsigned char* smem, const Stre
   unsigned char* tail = smem + static_cast<size_t>(pl.S) * pl.stage_bytes;
   L.full = reinterpret_cast<uint64_t*>(tail);
   L.xbar = L.full + kMaxStages;
-  L.xpart = reinterpret_cast<float*>(L.xbar + 2);
-  L.red = L.xpart + 2 * kMaxCluster;
+  L.xpart = reinterpret_cast<float*>(L.xbar + kXSlots);
+  L.red = L.xpart + kXSlots * kMaxCluster;
   L.bc = L.red + 64;
-  L.bcf = reinterpret_cast<int*>(L.bc + 2);
+  L.bcf = reinterpret_cast<int*>(L.bc + kXSlots);
   return L;
 }
 
 __device__ __forceinline__ void init_barriers(const SmemLayout& L, const StreamPlan& pl) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < pl.S; ++s) mbar_init(&L.full[s], 1);
-    mbar_init(&L.xbar[0], 1);
-    mbar_init(&L.xbar[1], 1);
+    for (int s = 0; s < kXSlots; ++s) mbar_init(&L.xbar[s], 1);
     fence_mbar_init();
   }
   __syncthreads();
   if (pl.P > 1) cluster_sync_all();
 }
 
-// Sum of `v` over the G threads of a whole-slice row group (G a multiple of 32), then over
-// the P CTAs of the cluster. Every thread of the group returns the same total (summed in
-// warp order, then in cluster-rank order, so every CTA of the cluster gets the same bits).
-// Returns false, uniformly over the group, when the cluster exchange gave up.
-__device__ __forceinline__ bool row_group_sum(float& v, const StreamPlan& pl, const SmemLayout& L,
-                                              int gid, int gl, uint32_t seq, uint32_t rank,
-                                              int site) {
+// Sum of `v` over the G threads of row group `gid` (G a multiple of 32). Every thread of
+// the group gets the same bits: lanes load the per-warp partials in warp order and run the
+// same shuffle tree.
+__device__ __forceinline__ float group_sum(float v, const StreamPlan& pl, const SmemLayout& L, int gid,
+                                           int gl, uint32_t seq) {
   v = warp_sum(v);
-  const uint32_t par = seq & 1u;
   if (pl.G > 32) {
     const int nw = pl.G >> 5;
-    float* red = L.red + par * 32 + gid * nw;
-    if ((gl & 31) == 0) red[gl >> 5] = v;
+    const int lane = gl & 31;
+    float* red = L.red + (seq & 1u) * 32 + gid * nw;
+    if (lane == 0) red[gl >> 5] = v;
     named_barrier(1 + gid, pl.G);
-    float t = 0.f;
-    for (int j = 0; j < nw; ++j) t += red[j];
-    v = t;
+    v = warp_sum(lane < nw ? red[lane] : 0.f);
   }
-  if (pl.P > 1) {
-    const uint32_t parity = (seq >> 1) & 1u;
-    float* xp = L.xpart + par * kMaxCluster;
-    if (gl == 0) {
-      xp[rank] = v;
-      mbar_arrive_expect_tx(&L.xbar[par], static_cast<uint32_t>(pl.P - 1) * 4u);
-      const uint32_t my_slot = smem_u32(&xp[rank]);
-      const uint32_t my_bar = smem_u32(&L.xbar[par]);
-      for (int q = 0; q < pl.P; ++q) {
-        if (q == static_cast<int>(rank)) continue;
-        st_async_peer(map_peer(my_slot, q), v, map_peer(my_bar, q));
-      }
-      const bool ok = mbar_wait<true>(&L.xbar[par], parity, site);
-      float t = 0.f;
-      for (int q = 0; q < pl.P; ++q) t += xp[q];
-      L.bc[par] = t;
-      L.bcf[par] = ok ? 1 : 0;
+  return v;
+}
+
+// Sum of the group totals of the P CTAs of the cluster, in rank order (every CTA gets the
+// same bits). One thread sends this CTA's total into every peer's shared memory with
+// st.async (completing 4 tx-bytes on the peer's mbarrier), waits (bounded) for the peers'
+// totals, and broadcasts the result to the group. Returns false, uniformly over the
+// group, when the exchange gave up.
+__device__ __forceinline__ bool cluster_sum(float& v, const StreamPlan& pl, const SmemLayout& L, int gid,
+                                            int gl, uint32_t seq, uint32_t rank, int site) {
+  const uint32_t slot = seq & (kXSlots - 1);
+  const uint32_t parity = (seq / kXSlots) & 1u;
+  float* xp = L.xpart + slot * kMaxCluster;
+  if (gl == 0) {
+    xp[rank] = v;
+    mbar_arrive_expect_tx(&L.xbar[slot], static_cast<uint32_t>(pl.P - 1) * 4u);
+    const uint32_t my_slot = smem_u32(&xp[rank]);
+    const uint32_t my_bar = smem_u32(&L.xbar[slot]);
+    for (int q = 0; q < pl.P; ++q) {
+      if (q == static_cast<int>(rank)) continue;
+      st_async_peer(map_peer(my_slot, q), v, map_peer(my_bar, q));
     }
-    if (pl.G > 32) named_barrier(1 + gid, pl.G); else __syncwarp();
-    v = L.bc[par];
-    return L.bcf[par] != 0;
+    const bool ok = mbar_wait<true>(&L.xbar[slot], parity, site);
+    float t = 0.f;
+    for (int q = 0; q < pl.P; ++q) t += xp[q];
+    L.bc[slot] = t;
+    L.bcf[slot] = ok ? 1 : 0;
   }
-  return true;
+  if (pl.G > 32) named_barrier(1 + gid, pl.G); else __syncwarp();
+  v = L.bc[slot];
+  return L.bcf[slot] != 0;
 }
 
 // xor-shuffle sum over aligned groups of `width` lanes (width a power of two <= 32).
@@ -106,17 +117,15 @@ __device__ __forceinline__ float seg_sum(float v, int width, unsigned mask) {
   return v;
 }
 
-// Ring bookkeeping for thread 0: issues tiles in order and remembers how many it issued.
-struct Ring {
-  int64_t issued = 0;  // tiles issued so far (index in this cluster's tile sequence)
-};
-
 // Waits (bounded) for the copies of tiles [consumed, issued) after a failure.
 __device__ __forceinline__ void drain_ring(const StreamPlan& pl, const SmemLayout& L, int64_t consumed,
                                            int64_t issued) {
   for (int64_t j = consumed; j < issued; ++j)
     mbar_wait(&L.full[j % pl.S], static_cast<uint32_t>(j / pl.S) & 1u, kSiteDrain);
 }
+
+template <typename T>
+using Elt = typename std::conditional<Present<T>::value, T, float>::type;
 
 // =======================================================================================
 // Forward
@@ -130,21 +139,26 @@ __device__ __forceinline__ void fwd_issue(const FwdParams& p, const StreamPlan& 
   const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
   fence_proxy_async_smem();
   const uint32_t bx = static_cast<uint32_t>(rows) * pl.row_bytes[0];
-  const uint32_t br = p.res != nullptr ? static_cast<uint32_t>(rows) * pl.row_bytes[1] : 0u;
+  const uint32_t br = Present<RT>::value ? static_cast<uint32_t>(rows) * pl.row_bytes[1] : 0u;
   mbar_arrive_expect_tx(&L.full[s], bx + br);
   const int64_t e0 = row0 * pl.W + slice_elt0;  // P > 1 implies R == 1
   bulk_load(st + pl.off[0], static_cast<const X*>(p.x) + e0, bx, &L.full[s], pol);
-  if (p.res != nullptr)
+  if constexpr (Present<RT>::value)
     bulk_load(st + pl.off[1], static_cast<const RT*>(p.res) + e0, br, &L.full[s], pol);
 }
 
-template <typename X, typename RT>
-__global__ void __launch_bounds__(kBlockThreads, 1) fwd_stream_kernel(const FwdParams p) {
+// X: input dtype; RT: residual dtype (NoT = none); OT: output dtype; ROT: residual_out
+// dtype (NoT = not written).
+template <typename X, typename RT, typename OT, typename ROT, int kVecs, int kBlock, int kMinBlocks>
+__global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const FwdParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
+  constexpr bool kRes = Present<RT>::value;
+  constexpr bool kRO = Present<ROT>::value;
+  using RTe = Elt<RT>;
+  using ROe = Elt<ROT>;
   const StreamPlan& pl = p.pl;
   const SmemLayout L = carve_smem(smem, pl);
   const int tid = threadIdx.x;
-  const int lane = tid & 31;
   uint32_t rank = 0;
   int64_t cid = blockIdx.x;
   int64_t ncl = gridDim.x;
@@ -155,12 +169,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) fwd_stream_kernel(const FwdP
   }
   init_barriers(L, pl);
 
-  const bool has_res = p.res != nullptr;
-  constexpr int sx = sizeof(X);
-  constexpr int sr = sizeof(RT);
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const uint64_t pol = l2_policy_evict_first();
-
   int64_t issued = 0;
   if (tid == 0) {
     for (int j = 0; j < pl.S; ++j) {
@@ -171,26 +181,32 @@ __global__ void __launch_bounds__(kBlockThreads, 1) fwd_stream_kernel(const FwdP
     }
   }
 
-  const int gid = tid / pl.G;
-  const int gl = tid - gid * pl.G;
+  const int G = pl.G;
+  const int G8 = G * 8;
+  const int gid = tid / G;
+  const int gl = tid - gid * G;
   const bool in_group = gid < pl.rps;
-  const int N = pl.N;
-  const float n_f = static_cast<float>(N);
+  const float n_f = static_cast<float>(pl.N);
+  unsigned vmask = 0;
+#pragma unroll
+  for (int k = 0; k < kVecs; ++k)
+    if (in_group && gl + k * G < pl.vslice) vmask |= 1u << k;
 
-  float wr[kMaxVecs][8];
-  float br_[kMaxVecs][8];
+  float wr[kVecs][8];
+  float br[kVecs][8];
 #pragma unroll
-  for (int k = 0; k < kMaxVecs; ++k) {
-    const int v = gl + k * pl.G;
-    const int64_t c = slice_elt0 + static_cast<int64_t>(v) * 8;
-    const bool valid = in_group && v < pl.vslice;
+  for (int k = 0; k < kVecs; ++k) {
+    const int64_t c = slice_elt0 + static_cast<int64_t>(gl + k * G) * 8;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) { wr[k][e] = 1.f; br_[k][e] = 0.f; }
-    if (valid && p.w != nullptr) load8_rt(p.w, p.w_dt, p.w_per_head ? c : c % N, wr[k], true);
-    if (valid && p.b != nullptr) load8_rt(p.b, p.b_dt, p.b_per_head ? c : c % N, br_[k], true);
+    for (int e = 0; e < 8; ++e) { wr[k][e] = 1.f; br[k][e] = 0.f; }
+    if ((vmask >> k) & 1u) {
+      if (p.w != nullptr) load8_rt(p.w, p.w_dt, p.w_per_head ? c : c % pl.N, wr[k], true);
+      if (p.b != nullptr) load8_rt(p.b, p.b_dt, p.b_per_head ? c : c % pl.N, br[k], true);
+    }
   }
 
-  uint32_t seq = 0;  // rows processed by this group (parity of scratch slots, cluster phases)
+  const int xs_stride = static_cast<int>(pl.row_bytes[0] / sizeof(X));  // elements per staged row
+  uint32_t seq = 0;  // rows reduced by this group (parity of scratch slots, cluster phases)
   int64_t i = 0;
   bool failed = false;
   for (int64_t tile = cid; tile < pl.ntiles; tile += ncl, ++i) {
@@ -199,9 +215,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1) fwd_stream_kernel(const FwdP
     if (__syncthreads_or(!ok || failed)) { failed = true; break; }
     if (tid == 0 && i > 0 && pl.S > 1) {  // everyone is past tile i-1: its stage is free
       const int64_t t = cid + (i - 1 + pl.S) * ncl;
-      if (t < pl.ntiles) { fwd_issue<X, RT>(p, pl, L, smem, t, static_cast<int>((i - 1) % pl.S), slice_elt0, pol); ++issued; }
+      if (t < pl.ntiles) {
+        fwd_issue<X, RT>(p, pl, L, smem, t, static_cast<int>((i - 1) % pl.S), slice_elt0, pol);
+        ++issued;
+      }
     }
     const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
+    const X* xs0 = reinterpret_cast<const X*>(st + pl.off[0]) + gl * 8;
+    const RTe* rs0 = reinterpret_cast<const RTe*>(st + pl.off[1]) + gl * 8;
     const int64_t row0 = tile * pl.R;
     const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
     for (int sw = 0; sw < pl.R; sw += pl.rps) {
@@ -209,75 +230,79 @@ __global__ void __launch_bounds__(kBlockThreads, 1) fwd_stream_kernel(const FwdP
       const bool active = in_group && lr < rows;
       const unsigned amask = __ballot_sync(0xffffffffu, active);
       if (!active) continue;
-      const unsigned char* xs = st + pl.off[0] + static_cast<size_t>(lr) * pl.row_bytes[0];
-      const unsigned char* rs = st + pl.off[1] + static_cast<size_t>(lr) * pl.row_bytes[1];
+      const X* xs = xs0 + lr * xs_stride;
+      const RTe* rs = rs0 + lr * xs_stride;
       const int64_t row = row0 + lr;
-      const int64_t g0 = row * pl.W + slice_elt0;  // global element index of the slice
+      const int64_t g0 = row * pl.W + slice_elt0 + gl * 8;
 
-      float part[kMaxVecs];
+      float part[kVecs];
 #pragma unroll
-      for (int k = 0; k < kMaxVecs; ++k) {
-        const int v = gl + k * pl.G;
-        float acc = 0.f;
-        if (v < pl.vslice) {
+      for (int k = 0; k < kVecs; ++k) {
+        part[k] = 0.f;
+        if ((vmask >> k) & 1u) {
           float h[8];
-          Vec8<X>::load(xs + v * 8 * sx, h);
-          if (has_res) {
+          Vec8<X>::load(xs + k * G8, h);
+          if constexpr (kRes) {
             float r[8];
-            Vec8<RT>::load(rs + v * 8 * sr, r);
+            Vec8<RTe>::load(rs + k * G8, r);
 #pragma unroll
             for (int e = 0; e < 8; ++e) h[e] += r[e];
           }
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc = fmaf(h[e], h[e], acc);
+          for (int e = 0; e < 8; ++e) part[k] = fmaf(h[e], h[e], part[k]);
         }
-        part[k] = acc;
       }
 
-      float rstd_k[kMaxVecs];
+      float rstd_k[kVecs];
       if (pl.seg_mode) {
 #pragma unroll
-        for (int k = 0; k < kMaxVecs; ++k) {
-          const float ss = seg_sum(part[k], pl.vs, amask);
-          rstd_k[k] = rsqrtf(ss / n_f + p.eps);
-        }
+        for (int k = 0; k < kVecs; ++k) rstd_k[k] = rsqrtf(seg_sum(part[k], pl.vs, amask) / n_f + p.eps);
       } else {
         float ss = 0.f;
 #pragma unroll
-        for (int k = 0; k < kMaxVecs; ++k) ss += part[k];
-        const bool red_ok = row_group_sum(ss, pl, L, gid, gl, seq, rank, kSiteFwdCluster);
+        for (int k = 0; k < kVecs; ++k) ss += part[k];
+        ss = group_sum(ss, pl, L, gid, gl, seq);
+        if (pl.P > 1 && !cluster_sum(ss, pl, L, gid, gl, seq, rank, kSiteFwdCluster)) {
+          failed = true;
+          ++seq;
+          break;
+        }
         ++seq;
-        if (!red_ok) { failed = true; break; }
         const float r = rsqrtf(ss / n_f + p.eps);
 #pragma unroll
-        for (int k = 0; k < kMaxVecs; ++k) rstd_k[k] = r;
+        for (int k = 0; k < kVecs; ++k) rstd_k[k] = r;
       }
 
+      OT* op = static_cast<OT*>(p.out) + g0;
+      ROe* rop = static_cast<ROe*>(p.ro) + g0;
 #pragma unroll
-      for (int k = 0; k < kMaxVecs; ++k) {
-        const int v = gl + k * pl.G;
-        if (v < pl.vslice) {
+      for (int k = 0; k < kVecs; ++k) {
+        if ((vmask >> k) & 1u) {
           float h[8];
-          Vec8<X>::load(xs + v * 8 * sx, h);
-          if (has_res) {
+          Vec8<X>::load(xs + k * G8, h);
+          if constexpr (kRes) {
             float r[8];
-            Vec8<RT>::load(rs + v * 8 * sr, r);
+            Vec8<RTe>::load(rs + k * G8, r);
 #pragma unroll
             for (int e = 0; e < 8; ++e) h[e] += r[e];
           }
-          const int64_t ge = g0 + static_cast<int64_t>(v) * 8;
-          if (p.ro != nullptr) store8_rt(p.ro, p.ro_dt, ge, h);
+          if constexpr (kRO) Vec8<ROe>::store(rop + k * G8, h);
           float y[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) y[e] = fmaf(h[e] * rstd_k[k], wr[k][e], br_[k][e]);
-          store8_rt(p.out, p.out_dt, ge, y);
-          if (p.rstd != nullptr) {
-            if (pl.seg_mode) {
-              if ((v & (pl.vs - 1)) == 0) p.rstd[row * pl.heads + v / pl.vs] = rstd_k[k];
-            } else if (v == 0 && rank == 0) {
-              p.rstd[row] = rstd_k[k];
-            }
+          for (int e = 0; e < 8; ++e) y[e] = fmaf(h[e] * rstd_k[k], wr[k][e], br[k][e]);
+          Vec8<OT>::store(op + k * G8, y);
+        }
+      }
+      if (p.rstd != nullptr) {
+        if (pl.seg_mode) {
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) {
+            const int v = gl + k * G;
+            if (((vmask >> k) & 1u) && (v & (pl.vs - 1)) == 0)
+              p.rstd[row * pl.heads + (v >> pl.vs_shift)] = rstd_k[k];
           }
+        } else if (gl == 0 && rank == 0) {
+          p.rstd[row] = rstd_k[0];
         }
       }
     }
@@ -289,17 +314,15 @@ __global__ void __launch_bounds__(kBlockThreads, 1) fwd_stream_kernel(const FwdP
   }
   failed = __syncthreads_or(failed);
   if (failed && tid == 0) drain_ring(pl, L, i, issued);
-  (void)lane;
 }
 
 // =======================================================================================
 // Backward: dx in one pass from the saved rstd; dweight / dbias per-CTA partial rows.
 // =======================================================================================
-template <typename X, typename DY>
+template <typename X, typename DY, typename DROT>
 __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& pl, const SmemLayout& L,
                                           unsigned char* smem, int64_t tile, int s,
-                                          int64_t slice_elt0, int rstd_per_row, int sdro,
-                                          uint64_t pol) {
+                                          int64_t slice_elt0, int rstd_per_row, uint64_t pol) {
   unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
   const int64_t row0 = tile * pl.R;
   const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
@@ -315,18 +338,25 @@ __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& 
   cp_async_arrive(&L.full[s]);
   const uint32_t b0 = static_cast<uint32_t>(rows) * pl.row_bytes[0];
   const uint32_t b1 = static_cast<uint32_t>(rows) * pl.row_bytes[1];
-  const uint32_t b2 = p.dro != nullptr ? static_cast<uint32_t>(rows) * pl.row_bytes[2] : 0u;
+  const uint32_t b2 = Present<DROT>::value ? static_cast<uint32_t>(rows) * pl.row_bytes[2] : 0u;
   mbar_arrive_expect_tx(&L.full[s], b0 + b1 + b2);
   const int64_t e0 = row0 * pl.W + slice_elt0;
   bulk_load(st + pl.off[0], static_cast<const X*>(p.x) + e0, b0, &L.full[s], pol);
   bulk_load(st + pl.off[1], static_cast<const DY*>(p.dy) + e0, b1, &L.full[s], pol);
-  if (p.dro != nullptr)
-    bulk_load(st + pl.off[2], static_cast<const unsigned char*>(p.dro) + e0 * sdro, b2, &L.full[s], pol);
+  if constexpr (Present<DROT>::value)
+    bulk_load(st + pl.off[2], static_cast<const DROT*>(p.dro) + e0, b2, &L.full[s], pol);
 }
 
-template <typename X, typename DY, bool kHasDb, int kVecs>
-__global__ void __launch_bounds__(kBlockThreads, 1) bwd_stream_kernel(const BwdParams p) {
+// X: saved input dtype; DY: dout dtype; DXT: dx dtype; DROT: dresidual_out dtype (NoT =
+// none); DREST: dresidual dtype (NoT = not written).
+template <typename X, typename DY, typename DXT, typename DROT, typename DREST, bool kHasDb, int kVecs,
+          int kBlock, int kMinBlocks>
+__global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const BwdParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
+  constexpr bool kDro = Present<DROT>::value;
+  constexpr bool kDres = Present<DREST>::value;
+  using DROe = Elt<DROT>;
+  using DRESe = Elt<DREST>;
   const StreamPlan& pl = p.pl;
   const SmemLayout L = carve_smem(smem, pl);
   const int tid = threadIdx.x;
@@ -340,47 +370,46 @@ __global__ void __launch_bounds__(kBlockThreads, 1) bwd_stream_kernel(const BwdP
   }
   init_barriers(L, pl);
 
-  const bool has_dro = p.dro != nullptr;
-  constexpr int sx = sizeof(X);
-  constexpr int sd = sizeof(DY);
-  const int sdro = has_dro ? dtype_bytes(p.dro_dt) : 0;
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const int rstd_per_row = pl.seg_mode ? pl.heads : 1;
   const uint64_t pol = l2_policy_evict_first();
-
   int64_t issued = 0;
   if (tid == 0) {
     for (int j = 0; j < pl.S; ++j) {
       const int64_t t = cid + j * ncl;
       if (t >= pl.ntiles) break;
-      bwd_issue<X, DY>(p, pl, L, smem, t, j, slice_elt0, rstd_per_row, sdro, pol);
+      bwd_issue<X, DY, DROT>(p, pl, L, smem, t, j, slice_elt0, rstd_per_row, pol);
       ++issued;
     }
   }
 
-  const int gid = tid / pl.G;
-  const int gl = tid - gid * pl.G;
+  const int G = pl.G;
+  const int G8 = G * 8;
+  const int gid = tid / G;
+  const int gl = tid - gid * G;
   const bool in_group = gid < pl.rps;
-  const int N = pl.N;
-  const float n_f = static_cast<float>(N);
-  const bool has_w = p.w != nullptr;
+  const float n_f = static_cast<float>(pl.N);
+  unsigned vmask = 0;
+#pragma unroll
+  for (int k = 0; k < kVecs; ++k)
+    if (in_group && gl + k * G < pl.vslice) vmask |= 1u << k;
 
   float wr[kVecs][8];
   float dw[kVecs][8];
   float db[kHasDb ? kVecs : 1][8];
 #pragma unroll
   for (int k = 0; k < kVecs; ++k) {
-    const int v = gl + k * pl.G;
-    const int64_t c = slice_elt0 + static_cast<int64_t>(v) * 8;
+    const int64_t c = slice_elt0 + static_cast<int64_t>(gl + k * G) * 8;
 #pragma unroll
     for (int e = 0; e < 8; ++e) { wr[k][e] = 1.f; dw[k][e] = 0.f; }
-    if (kHasDb) {
+    if constexpr (kHasDb) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) db[kHasDb ? k : 0][e] = 0.f;
     }
-    if (in_group && v < pl.vslice && has_w) load8_rt(p.w, p.w_dt, p.w_per_head ? c : c % N, wr[k], true);
+    if (((vmask >> k) & 1u) && p.w != nullptr) load8_rt(p.w, p.w_dt, p.w_per_head ? c : c % pl.N, wr[k], true);
   }
 
+  const int x_stride = static_cast<int>(pl.row_bytes[0] / sizeof(X));
   uint32_t seq = 0;
   int64_t i = 0;
   bool failed = false;
@@ -391,11 +420,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1) bwd_stream_kernel(const BwdP
     if (tid == 0 && i > 0 && pl.S > 1) {
       const int64_t t = cid + (i - 1 + pl.S) * ncl;
       if (t < pl.ntiles) {
-        bwd_issue<X, DY>(p, pl, L, smem, t, static_cast<int>((i - 1) % pl.S), slice_elt0, rstd_per_row, sdro, pol);
+        bwd_issue<X, DY, DROT>(p, pl, L, smem, t, static_cast<int>((i - 1) % pl.S), slice_elt0, rstd_per_row, pol);
         ++issued;
       }
     }
     const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
+    const X* xs0 = reinterpret_cast<const X*>(st + pl.off[0]) + gl * 8;
+    const DY* ds0 = reinterpret_cast<const DY*>(st + pl.off[1]) + gl * 8;
+    const DROe* as0 = reinterpret_cast<const DROe*>(st + pl.off[2]) + gl * 8;
     const float* rs_stage = reinterpret_cast<const float*>(st + pl.off[3]);
     const int64_t row0 = tile * pl.R;
     const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
@@ -404,34 +436,31 @@ __global__ void __launch_bounds__(kBlockThreads, 1) bwd_stream_kernel(const BwdP
       const bool active = in_group && lr < rows;
       const unsigned amask = __ballot_sync(0xffffffffu, active);
       if (!active) continue;
-      const unsigned char* xs = st + pl.off[0] + static_cast<size_t>(lr) * pl.row_bytes[0];
-      const unsigned char* ds = st + pl.off[1] + static_cast<size_t>(lr) * pl.row_bytes[1];
-      const unsigned char* as = st + pl.off[2] + static_cast<size_t>(lr) * pl.row_bytes[2];
-      const int64_t row = row0 + lr;
-      const int64_t g0 = row * pl.W + slice_elt0;
+      const X* xs = xs0 + lr * x_stride;
+      const DY* ds = ds0 + lr * x_stride;
+      const DROe* as = as0 + lr * x_stride;
+      const int64_t g0 = (row0 + lr) * pl.W + slice_elt0 + gl * 8;
 
       float rstd_k[kVecs];
       float part[kVecs];
 #pragma unroll
       for (int k = 0; k < kVecs; ++k) {
-        const int v = gl + k * pl.G;
-        float acc = 0.f;
+        part[k] = 0.f;
         rstd_k[k] = 0.f;
-        if (v < pl.vslice) {
-          const float r = rs_stage[lr * rstd_per_row + (pl.seg_mode ? v / pl.vs : 0)];
+        if ((vmask >> k) & 1u) {
+          const float r = rs_stage[lr * rstd_per_row + (pl.seg_mode ? ((gl + k * G) >> pl.vs_shift) : 0)];
           rstd_k[k] = r;
           float xv[8], dv[8];
-          Vec8<X>::load(xs + v * 8 * sx, xv);
-          Vec8<DY>::load(ds + v * 8 * sd, dv);
+          Vec8<X>::load(xs + k * G8, xv);
+          Vec8<DY>::load(ds + k * G8, dv);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float xh = xv[e] * r;
-            acc = fmaf(xh, dv[e] * wr[k][e], acc);
+            part[k] = fmaf(xh, dv[e] * wr[k][e], part[k]);
             dw[k][e] = fmaf(dv[e], xh, dw[k][e]);
-            if (kHasDb) db[kHasDb ? k : 0][e] += dv[e];
+            if constexpr (kHasDb) db[kHasDb ? k : 0][e] += dv[e];
           }
         }
-        part[k] = acc;
       }
 
       float c_k[kVecs];
@@ -442,33 +471,37 @@ __global__ void __launch_bounds__(kBlockThreads, 1) bwd_stream_kernel(const BwdP
         float dot = 0.f;
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) dot += part[k];
-        const bool red_ok = row_group_sum(dot, pl, L, gid, gl, seq, rank, kSiteBwdCluster);
+        dot = group_sum(dot, pl, L, gid, gl, seq);
+        if (pl.P > 1 && !cluster_sum(dot, pl, L, gid, gl, seq, rank, kSiteBwdCluster)) {
+          failed = true;
+          ++seq;
+          break;
+        }
         ++seq;
-        if (!red_ok) { failed = true; break; }
         const float c = dot / n_f;
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) c_k[k] = c;
       }
 
+      DXT* dxp = static_cast<DXT*>(p.dx) + g0;
+      DRESe* drp = static_cast<DRESe*>(p.dres) + g0;
 #pragma unroll
       for (int k = 0; k < kVecs; ++k) {
-        const int v = gl + k * pl.G;
-        if (v < pl.vslice) {
+        if ((vmask >> k) & 1u) {
           const float r = rstd_k[k];
           float xv[8], dv[8], g[8];
-          Vec8<X>::load(xs + v * 8 * sx, xv);
-          Vec8<DY>::load(ds + v * 8 * sd, dv);
+          Vec8<X>::load(xs + k * G8, xv);
+          Vec8<DY>::load(ds + k * G8, dv);
 #pragma unroll
           for (int e = 0; e < 8; ++e) g[e] = (dv[e] * wr[k][e] - (xv[e] * r) * c_k[k]) * r;
-          if (has_dro) {
+          if constexpr (kDro) {
             float a[8];
-            load8_rt(as + v * 8 * sdro, p.dro_dt, 0, a, false);
+            Vec8<DROe>::load(as + k * G8, a);
 #pragma unroll
             for (int e = 0; e < 8; ++e) g[e] += a[e];
           }
-          const int64_t ge = g0 + static_cast<int64_t>(v) * 8;
-          store8_rt(p.dx, p.dx_dt, ge, g);
-          if (p.dres != nullptr) store8_rt(p.dres, p.dres_dt, ge, g);
+          Vec8<DXT>::store(dxp + k * G8, g);
+          if constexpr (kDres) Vec8<DRESe>::store(drp + k * G8, g);
         }
       }
     }
@@ -476,7 +509,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) bwd_stream_kernel(const BwdP
       __syncthreads();
       const int64_t t = cid + (i + 1) * ncl;
       if (tid == 0 && t < pl.ntiles) {
-        bwd_issue<X, DY>(p, pl, L, smem, t, 0, slice_elt0, rstd_per_row, sdro, pol);
+        bwd_issue<X, DY, DROT>(p, pl, L, smem, t, 0, slice_elt0, rstd_per_row, pol);
         ++issued;
       }
     }
@@ -489,14 +522,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1) bwd_stream_kernel(const BwdP
 
   // one partial row per (cluster, row group): the groups of a CTA own the same columns.
   // Every owned column is written, zeros included, so the reduction reads no stale data.
-  const int64_t prow = (cid * pl.rps + gid) * pl.W;
+  const int64_t pbase = (cid * pl.rps + gid) * pl.W + slice_elt0 + gl * 8;
 #pragma unroll
   for (int k = 0; k < kVecs; ++k) {
-    const int v = gl + k * pl.G;
-    if (in_group && v < pl.vslice) {
-      const int64_t c = slice_elt0 + static_cast<int64_t>(v) * 8;
-      if (p.dw_part != nullptr) Vec8<float>::store(p.dw_part + prow + c, dw[k]);
-      if (kHasDb && p.db_part != nullptr) Vec8<float>::store(p.db_part + prow + c, db[kHasDb ? k : 0]);
+    if ((vmask >> k) & 1u) {
+      if (p.dw_part != nullptr) Vec8<float>::store(p.dw_part + pbase + k * G8, dw[k]);
+      if constexpr (kHasDb) {
+        if (p.db_part != nullptr) Vec8<float>::store(p.db_part + pbase + k * G8, db[kHasDb ? k : 0]);
+      }
     }
   }
 }

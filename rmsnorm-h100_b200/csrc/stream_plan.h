@@ -23,6 +23,7 @@ struct StreamPlan {
   int32_t P;          // CTAs per cluster = slices per super-row
   int32_t seg_mode;   // 1: segments of `vs` vectors reduced with xor shuffles; 0: whole slice
   int32_t vs;         // segment length in vectors (seg_mode)
+  int32_t vs_shift;   // log2(vs)
   int32_t vslice;     // vectors per slice
   int32_t heads;      // H
   int32_t N;          // hidden size (segment length in elements)
@@ -36,8 +37,10 @@ struct StreamPlan {
 };
 
 constexpr int kMaxVecs = 4;          // vectors per thread per super-row slice
-constexpr int kConsumerThreads = 512;
-constexpr int kBlockThreads = kConsumerThreads;  // 512 threads -> up to 128 registers
+// Launch shapes: 512 threads x 1 CTA per SM, or 256 threads x 2 CTAs per SM (both give
+// each thread up to 128 registers).
+constexpr int kBlockLarge = 512;
+constexpr int kBlockSmall = 256;
 constexpr int kMaxStages = 8;
 constexpr int kMaxCluster = 16;
 constexpr int kSmemReserve = 1024;   // barriers + reduction scratch after the stages
@@ -51,7 +54,7 @@ struct FwdParams {
   void* out;
   void* ro;
   float* rstd;
-  int32_t w_dt, b_dt, out_dt, ro_dt;
+  int32_t w_dt, b_dt;
   int32_t w_per_head, b_per_head;  // 1 when the affine tensor is [H, N]
   float eps;
 };
@@ -67,7 +70,7 @@ struct BwdParams {
   void* dres;
   float* dw_part;   // [nclusters][W] fp32 or null
   float* db_part;   // [nclusters][W] fp32 or null
-  int32_t w_dt, dro_dt, dres_dt, dx_dt;
+  int32_t w_dt;
   int32_t w_per_head;
 };
 
