@@ -338,48 +338,49 @@ def run_reference_arm(args, w):
 
 
 def e2e_measure(w, t_dev, dev, steps, group):
-    """Public API with pinned host buffers: H2D inputs, rmsnorm call, D2H outputs, per step."""
-    import rmsnorm
+    """Public API with pinned host buffers (rmsnorm.host_pipeline.HostPipeline): every step
+    copies its inputs host->device, runs the kernels, and copies its results back, with
+    the copies of consecutive row chunks overlapped on both copy engines."""
     from rmsnorm.distributed import allreduce_sum_
+    from rmsnorm.host_pipeline import HostPipeline
 
     h = w.get("heads", 1)
-    host = {}
-    for k in ("x", "res", "dy"):
-        if t_dev.get(k) is not None:
-            host[k] = t_dev[k].cpu().pin_memory()
+    pipe = HostPipeline(dev, chunk_rows=max(h, min(w["rows"], (32 << 20) // (w["n"] * 2))))
+    host = {k: t_dev[k].cpu().pin_memory() for k in ("x", "res", "dy") if t_dev.get(k) is not None}
     wt, b = t_dev["w"], t_dev.get("b")
-    shape = (w["rows"] // h, h, w["n"]) if h > 1 else (w["rows"], w["n"])
     stream = torch.cuda.current_stream(dev)
-    dbuf = {k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in host.items()}
-    out_host = {}
-    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    rows, n = w["rows"], w["n"]
+    if w["kind"] == "fwd":
+        out_h = torch.empty((rows, n), dtype=w["dtype"], pin_memory=True)
+        ro_h = torch.empty((rows, n), dtype=w["ro"], pin_memory=True) if w["ro"] is not None else None
+        rstd = torch.empty(rows, dtype=F32, device=dev) if w["rstd"] else None
+        rstd_h = torch.empty(rows, dtype=F32, pin_memory=True) if w["rstd"] else None
 
-    def one():
-        for k, v in host.items():
-            dbuf[k].copy_(v, non_blocking=True)
-        if w["kind"] == "fwd":
-            x = dbuf["x"].view(shape)
-            res = dbuf["res"].view(shape) if "res" in dbuf else None
-            out, ro, rstd = rmsnorm.rmsnorm_fwd(x, wt, b, res, residual_dtype=w["ro"], store_rstd=w["rstd"])
-            outs = {"out": out, "ro": ro if res is not None else None, "rstd": rstd}
-        else:
-            x = dbuf["x"].view(shape)
-            dy = dbuf["dy"].view(shape)
-            dx, dw, db, _ = rmsnorm.rmsnorm_bwd(x, wt, dy, t_dev["rstd"].view(shape[:-1]), has_bias=w["bias"])
+        def one():
+            pipe.fwd(host["x"], wt, b, host.get("res"), residual_dtype=w["ro"], out=out_h, residual_out=ro_h,
+                     rstd=rstd)
+            if rstd is not None:
+                rstd_h.copy_(rstd, non_blocking=True)
+
+        d2h = out_h.numel() * out_h.element_size() + (ro_h.numel() * ro_h.element_size() if ro_h is not None else 0)
+        d2h += rows * 4 if rstd is not None else 0
+    else:
+        dx_h = torch.empty((rows, n), dtype=w["dtype"], pin_memory=True)
+        dw_h = torch.empty(wt.shape, dtype=F32, pin_memory=True)
+        db_h = torch.empty(wt.shape, dtype=F32, pin_memory=True) if w["bias"] else None
+
+        def one():
+            _, dw, db = pipe.bwd(host["x"], wt, host["dy"], t_dev["rstd"], has_bias=w["bias"], dx=dx_h)
             if group is not None:
                 allreduce_sum_([dw, db], group=group)
-            outs = {"dx": dx, "dw": dw, "db": db}
-        d2h = 0
-        for k, v in outs.items():
-            if v is None:
-                continue
-            if k not in out_host:
-                out_host[k] = torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
-            out_host[k].copy_(v, non_blocking=True)
-            d2h += v.numel() * v.element_size()
-        return d2h
+            dw_h.copy_(dw, non_blocking=True)
+            if db_h is not None:
+                db_h.copy_(db, non_blocking=True)
 
-    d2h = one()
+        d2h = dx_h.numel() * dx_h.element_size() + dw_h.numel() * 4 * (2 if db_h is not None else 1)
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+
+    one()
     torch.cuda.synchronize(dev)
     barrier(group)
     e0 = torch.cuda.Event(enable_timing=True)

@@ -124,21 +124,54 @@ __global__ void __launch_bounds__(kGenericThreads) bwd_generic_partials_kernel(
   if (db_part) db_part[static_cast<int64_t>(blockIdx.y) * W + j] = db;
 }
 
-// out[j] = sum_{c < C} sum_{h < fold} part[c][h * N + j], in exactly that order.
-// fold = H folds a per-head super-row back onto a shared [N] parameter; fold = 1 keeps
-// all W = H*N columns.
-__global__ void __launch_bounds__(kGenericThreads) reduce_partials_kernel(
-    const float* __restrict__ part, int64_t C, int64_t W, int64_t N, int32_t fold,
-    void* out, int32_t out_dt) {
+// out[j] = sum over partial rows c < C and heads h < fold of part[c][h * N + j], in a fixed
+// order: warp w of the block sums rows c = w, w + 8, w + 16, ... (heads innermost), then
+// the 8 warp sums are added in warp order. fold = H folds a per-head super-row back onto a
+// shared [N] parameter; fold = 1 keeps all W = H*N columns. One lane per column (32
+// columns per block), so every warp load is a coalesced 128-byte row segment.
+constexpr int kReduceCols = 32;
+constexpr int kReduceWarps = 8;
+constexpr int kReduceThreads = kReduceCols * kReduceWarps;
+
+__global__ void __launch_bounds__(kReduceThreads) reduce_partials_kernel(
+    const float* __restrict__ part, int64_t C, int64_t W, int64_t N, int32_t fold, void* out,
+    int32_t out_dt) {
+  __shared__ float acc_w[kReduceWarps][kReduceCols];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const int64_t wout = fold > 1 ? N : W;
-  const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (j >= wout) return;
+  const int64_t j = static_cast<int64_t>(blockIdx.x) * kReduceCols + lane;
   float acc = 0.f;
-  for (int64_t c = 0; c < C; ++c) {
-    const float* row = part + c * W;
-    for (int h = 0; h < fold; ++h) acc += row[h * N + j];
+  if (j < wout) {
+    int64_t c = warp;
+#pragma unroll 1
+    for (; c + 3 * kReduceWarps < C; c += 4 * kReduceWarps) {
+      // four rows per step: independent loads in flight, added in row order
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float* row = part + (c + u * kReduceWarps) * W + j;
+        float t = 0.f;
+        for (int h = 0; h < fold; ++h) t += row[h * N];
+        v[u] = t;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc += v[u];
+    }
+    for (; c < C; c += kReduceWarps) {
+      const float* row = part + c * W + j;
+      float t = 0.f;
+      for (int h = 0; h < fold; ++h) t += row[h * N];
+      acc += t;
+    }
   }
-  store1_rt(out, out_dt, j, acc);
+  acc_w[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && j < wout) {
+    float t = 0.f;
+    for (int w = 0; w < kReduceWarps; ++w) t += acc_w[w][lane];
+    store1_rt(out, out_dt, j, t);
+  }
 }
 
 // Failure-detection self test: one CTA waits on an mbarrier that nothing arrives at.

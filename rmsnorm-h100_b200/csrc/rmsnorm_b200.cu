@@ -208,6 +208,60 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
   pl.P = P;
   pl.rps = P > 1 ? 1 : T / pl.G;
   if (pl.rps < 1) { *why = "group wider than the CTA"; return false; }
+  pl.K = 1;
+  pl.lag = 0;
+  pl.kpc_shift = log2i(max_vecs);
+
+  if (P > 1) {
+    // Split-row pipeline: pick sub-chunks per slice K and the exchange lag that keep the
+    // most bytes loading while rows wait. Lag 1 keeps two rows resident (S >= 2K), lag 0
+    // one (S >= K); K > 1 needs every thread to own max_vecs vectors of the slice.
+    const bool full = pl.vslice == pl.G * max_vecs;
+    const int force_k = env_int("RMSNORM_B200_FORCE_K", 0);
+    const int force_lag = env_int("RMSNORM_B200_FORCE_LAG", -1);
+    int best_k = 0, best_lag = 0, best_s = 0;
+    int64_t best_score = -1;
+    uint32_t best_chunk = 0;
+    for (int k = 1; k <= 4 && k <= max_vecs; k <<= 1) {
+      if (max_vecs % k || (k > 1 && !full)) continue;
+      if (force_k && k != force_k) continue;
+      uint32_t chunk = 0;
+      for (int t = 0; t < 3; ++t) chunk = align_up(chunk + static_cast<uint32_t>(pl.vslice / k) * 8u * in_bytes[t], 128);
+      if (rstd_staged) chunk += 128;
+      const int s_max = std::min<int>(kMaxStages, budget / static_cast<int>(chunk));
+      for (int lag = 1; lag >= 0; --lag) {
+        if (force_lag >= 0 && lag != force_lag) continue;
+        if (s_max < (1 + lag) * k) continue;
+        const int64_t inflight = static_cast<int64_t>(s_max - (1 + lag) * k) * chunk;
+        const int64_t score = inflight + ((lag == 1 && inflight >= 64 * 1024) ? (int64_t(1) << 40) : 0);
+        if (score > best_score) {
+          best_score = score;
+          best_k = k;
+          best_lag = lag;
+          best_s = s_max;
+          best_chunk = chunk;
+        }
+      }
+    }
+    if (best_k == 0) { *why = "no split-row ring fits"; return false; }
+    pl.K = best_k;
+    pl.lag = best_lag;
+    pl.kpc_shift = log2i(max_vecs / best_k);
+    pl.R = 1;
+    uint32_t off = 0;
+    for (int t = 0; t < 3; ++t) {
+      pl.row_bytes[t] = static_cast<uint32_t>(pl.vslice / best_k) * 8u * in_bytes[t];
+      pl.off[t] = off;
+      off = align_up(off + pl.row_bytes[t], 128);
+    }
+    pl.off[3] = off;
+    pl.stage_bytes = best_chunk;
+    const int max_s = std::max(1, std::min(kMaxStages, env_int("RMSNORM_B200_MAX_STAGES", kMaxStages)));
+    pl.S = std::max((1 + best_lag) * best_k, std::min(best_s, max_s));
+    pl.ntiles = pl.nrows;
+    *out = pl;
+    return true;
+  }
 
   uint32_t per_row = 0;
   for (int k = 0; k < 3; ++k) {
@@ -255,9 +309,9 @@ std::string describe(const char* kind, const StreamPlan& pl, int grid) {
   char buf[512];
   std::snprintf(buf, sizeof(buf),
                 "%s mode=%s P=%d grid=%d clusters=%d T=%d G=%d rps=%d R=%d S=%d stage=%u "
-                "vslice=%d vs=%d tiles=%lld",
+                "vslice=%d vs=%d K=%d lag=%d tiles=%lld",
                 kind, pl.seg_mode ? "seg" : "row", pl.P, grid, pl.nclusters, pl.T, pl.G, pl.rps,
-                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, static_cast<long long>(pl.ntiles));
+                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, pl.K, pl.lag, static_cast<long long>(pl.ntiles));
   return buf;
 }
 
@@ -319,6 +373,9 @@ FwdKernel pick_fwd(int x, int r, int o, int ro) {
   RMSB_FWD(h16, H, h16, H, h16, H, float, F)
   RMSB_FWD(b16, B, float, F, b16, B, float, F)
   RMSB_FWD(h16, H, float, F, h16, H, float, F)
+  // out_dtype = float32 from half/bf16 inputs
+  RMSB_FWD(b16, B, NoT, NA, float, F, NoT, NA)
+  RMSB_FWD(h16, H, NoT, NA, float, F, NoT, NA)
 #undef RMSB_FWD
   return nullptr;
 }
@@ -359,6 +416,9 @@ BwdKernel pick_bwd(int x, int dy, int dx, int dro, int dres, bool db, bool small
   RMSB_BWD(float, F, h16, H, h16, H, NoT, NA, float, F)
   RMSB_BWD(float, F, b16, B, b16, B, float, F, float, F)
   RMSB_BWD(float, F, h16, H, h16, H, float, F, float, F)
+  // the public rmsnorm_bwd on a saved fp32 residual_out returns dx in the saved dtype
+  RMSB_BWD(float, F, b16, B, float, F, NoT, NA, NoT, NA)
+  RMSB_BWD(float, F, h16, H, float, F, NoT, NA, NoT, NA)
 #undef RMSB_BWD
 #undef RMSB_BWD_SHAPE
   return nullptr;
@@ -623,9 +683,9 @@ int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream
   auto reduce = [&](const float* part, void* outp, int out_dt, int out_heads) -> int {
     const int fold = (out_heads == 1 && a->heads > 1) ? a->heads : 1;
     const int64_t wout = fold > 1 ? a->hidden : bp.W;
-    const unsigned blocks = static_cast<unsigned>((wout + kGenericThreads - 1) / kGenericThreads);
-    reduce_partials_kernel<<<blocks, kGenericThreads, 0, stream>>>(part, nparts, bp.W, a->hidden, fold,
-                                                                  outp, out_dt);
+    const unsigned blocks = static_cast<unsigned>((wout + kReduceCols - 1) / kReduceCols);
+    reduce_partials_kernel<<<blocks, kReduceThreads, 0, stream>>>(part, nparts, bp.W, a->hidden, fold,
+                                                                 outp, out_dt);
     if (cudaGetLastError() != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return RMSNORM_B200_OK;

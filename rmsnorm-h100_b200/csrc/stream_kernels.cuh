@@ -111,6 +111,43 @@ __device__ __forceinline__ bool cluster_sum(float& v, const StreamPlan& pl, cons
   return L.bcf[slot] != 0;
 }
 
+// Split form of cluster_sum for the pipelined split-row loop: cluster_send posts this
+// CTA's total for row `seq` (thread gl == 0 only, no wait); cluster_recv waits (bounded)
+// for the peers' totals of row `seq`, sums them in rank order and broadcasts the result to
+// the group. Four slots (seq mod 4) make two rows in flight safe: a peer can only post row
+// seq + 4 after it received this CTA's row seq + 2, which this CTA sends after it has read
+// row seq.
+__device__ __forceinline__ void cluster_send(float v, const StreamPlan& pl, const SmemLayout& L, int gl,
+                                             uint32_t seq, uint32_t rank) {
+  if (gl != 0) return;
+  const uint32_t slot = seq & (kXSlots - 1);
+  float* xp = L.xpart + slot * kMaxCluster;
+  xp[rank] = v;
+  mbar_arrive_expect_tx(&L.xbar[slot], static_cast<uint32_t>(pl.P - 1) * 4u);
+  const uint32_t my_slot = smem_u32(&xp[rank]);
+  const uint32_t my_bar = smem_u32(&L.xbar[slot]);
+  for (int q = 0; q < pl.P; ++q) {
+    if (q == static_cast<int>(rank)) continue;
+    st_async_peer(map_peer(my_slot, q), v, map_peer(my_bar, q));
+  }
+}
+
+__device__ __forceinline__ bool cluster_recv(float& v, const StreamPlan& pl, const SmemLayout& L, int gid,
+                                             int gl, uint32_t seq, int site) {
+  const uint32_t slot = seq & (kXSlots - 1);
+  if (gl == 0) {
+    const bool ok = mbar_wait<true>(&L.xbar[slot], (seq / kXSlots) & 1u, site);
+    const float* xp = L.xpart + slot * kMaxCluster;
+    float t = 0.f;
+    for (int q = 0; q < pl.P; ++q) t += xp[q];
+    L.bc[slot] = t;
+    L.bcf[slot] = ok ? 1 : 0;
+  }
+  if (pl.G > 32) named_barrier(1 + gid, pl.G); else __syncwarp();
+  v = L.bc[slot];
+  return L.bcf[slot] != 0;
+}
+
 // xor-shuffle sum over aligned groups of `width` lanes (width a power of two <= 32).
 __device__ __forceinline__ float seg_sum(float v, int width, unsigned mask) {
   for (int off = width >> 1; off > 0; off >>= 1) v += __shfl_xor_sync(mask, v, off);
@@ -147,6 +184,22 @@ __device__ __forceinline__ void fwd_issue(const FwdParams& p, const StreamPlan& 
     bulk_load(st + pl.off[1], static_cast<const RT*>(p.res) + e0, br, &L.full[s], pol);
 }
 
+// Split-row pipeline: sub-chunk j of the row slice of tile `tile` into ring slot `slot`.
+template <typename X, typename RT>
+__device__ __forceinline__ void fwd_issue_chunk(const FwdParams& p, const StreamPlan& pl, const SmemLayout& L,
+                                                unsigned char* smem, int64_t tile, int j, int slot,
+                                                int64_t slice_elt0, uint64_t pol) {
+  unsigned char* st = smem + static_cast<size_t>(slot) * pl.stage_bytes;
+  fence_proxy_async_smem();
+  const uint32_t bx = pl.row_bytes[0];
+  const uint32_t br = Present<RT>::value ? pl.row_bytes[1] : 0u;
+  mbar_arrive_expect_tx(&L.full[slot], bx + br);
+  const int64_t e0 = tile * pl.W + slice_elt0 + static_cast<int64_t>(j) * (pl.vslice / pl.K) * 8;
+  bulk_load(st + pl.off[0], static_cast<const X*>(p.x) + e0, bx, &L.full[slot], pol);
+  if constexpr (Present<RT>::value)
+    bulk_load(st + pl.off[1], static_cast<const RT*>(p.res) + e0, br, &L.full[slot], pol);
+}
+
 // X: input dtype; RT: residual dtype (NoT = none); OT: output dtype; ROT: residual_out
 // dtype (NoT = not written).
 template <typename X, typename RT, typename OT, typename ROT, int kVecs, int kBlock, int kMinBlocks>
@@ -172,7 +225,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const uint64_t pol = l2_policy_evict_first();
   int64_t issued = 0;
-  if (tid == 0) {
+  if (tid == 0 && pl.P == 1) {
     for (int j = 0; j < pl.S; ++j) {
       const int64_t t = cid + j * ncl;
       if (t >= pl.ntiles) break;
@@ -203,6 +256,115 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       if (p.w != nullptr) load8_rt(p.w, p.w_dt, p.w_per_head ? c : c % pl.N, wr[k], true);
       if (p.b != nullptr) load8_rt(p.b, p.b_dt, p.b_per_head ? c : c % pl.N, br[k], true);
     }
+  }
+
+  if (pl.P > 1) {
+    // ------------- split-row pipeline (row slices across a cluster, R = 1) -------------
+    // Row slices are streamed as K sub-chunks through an S-slot ring. Iteration i runs
+    // pass 1 of row i and posts its partial sum to the cluster, then (lag 1) receives
+    // row i-1's total and runs its pass 2, so the exchange overlaps a whole pass 1.
+    const int K = pl.K;
+    const int kpc_mask = (1 << pl.kpc_shift) - 1;
+    const int64_t n_local = cid < pl.ntiles ? (pl.ntiles - 1 - cid) / ncl + 1 : 0;
+    const int64_t total_q = n_local * K;
+    const bool grp = tid < G;
+    if (tid == 0) {
+      while (issued < min(total_q, static_cast<int64_t>(pl.S))) {
+        const int64_t r = issued / K;
+        fwd_issue_chunk<X, RT>(p, pl, L, smem, cid + r * ncl, static_cast<int>(issued - r * K),
+                               static_cast<int>(issued % pl.S), slice_elt0, pol);
+        ++issued;
+      }
+    }
+    auto xptr = [&](int64_t row_local, int k) -> const X* {
+      const int64_t q = row_local * K + (k >> pl.kpc_shift);
+      return reinterpret_cast<const X*>(smem + static_cast<size_t>(q % pl.S) * pl.stage_bytes + pl.off[0]) +
+             (gl + (k & kpc_mask) * G) * 8;
+    };
+    auto rptr = [&](int64_t row_local, int k) -> const RTe* {
+      const int64_t q = row_local * K + (k >> pl.kpc_shift);
+      return reinterpret_cast<const RTe*>(smem + static_cast<size_t>(q % pl.S) * pl.stage_bytes + pl.off[1]) +
+             (gl + (k & kpc_mask) * G) * 8;
+    };
+    bool failed = false;
+    int64_t i = 0;
+    for (; i < n_local + pl.lag; ++i) {
+      bool ok = true;
+      if (i < n_local) {
+        for (int j = 0; j < K; ++j) {
+          const int64_t q = i * K + j;
+          ok = mbar_wait(&L.full[q % pl.S], static_cast<uint32_t>(q / pl.S) & 1u, kSiteFwdFull) && ok;
+        }
+      }
+      if (__syncthreads_or(!ok || failed)) { failed = true; break; }
+      if (grp) {
+        if (i < n_local) {
+          float ss = 0.f;
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) {
+            if ((vmask >> k) & 1u) {
+              float h[8];
+              Vec8<X>::load(xptr(i, k), h);
+              if constexpr (kRes) {
+                float r[8];
+                Vec8<RTe>::load(rptr(i, k), r);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) h[e] += r[e];
+              }
+#pragma unroll
+              for (int e = 0; e < 8; ++e) ss = fmaf(h[e], h[e], ss);
+            }
+          }
+          ss = group_sum(ss, pl, L, 0, gl, static_cast<uint32_t>(i));
+          cluster_send(ss, pl, L, gl, static_cast<uint32_t>(i), rank);
+        }
+        const int64_t r2 = i - pl.lag;
+        if (r2 >= 0 && r2 < n_local) {
+          float tot;
+          if (!cluster_recv(tot, pl, L, 0, gl, static_cast<uint32_t>(r2), kSiteFwdCluster)) {
+            failed = true;
+          } else {
+            const float rs = rsqrtf(tot / n_f + p.eps);
+            const int64_t row = cid + r2 * ncl;
+            const int64_t g0 = row * pl.W + slice_elt0 + gl * 8;
+            OT* op = static_cast<OT*>(p.out) + g0;
+            ROe* rop = static_cast<ROe*>(p.ro) + g0;
+#pragma unroll
+            for (int k = 0; k < kVecs; ++k) {
+              if ((vmask >> k) & 1u) {
+                float h[8];
+                Vec8<X>::load(xptr(r2, k), h);
+                if constexpr (kRes) {
+                  float r[8];
+                  Vec8<RTe>::load(rptr(r2, k), r);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) h[e] += r[e];
+                }
+                if constexpr (kRO) Vec8<ROe>::store(rop + k * G8, h);
+                float y[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) y[e] = fmaf(h[e] * rs, wr[k][e], br[k][e]);
+                Vec8<OT>::store(op + k * G8, y);
+              }
+            }
+            if (p.rstd != nullptr && gl == 0 && rank == 0) p.rstd[row] = rs;
+          }
+        }
+      }
+      __syncthreads();  // pass 2 of row i - lag is done: its slots are free
+      if (tid == 0) {
+        const int64_t lim = min(total_q, max(static_cast<int64_t>(0), i + 1 - pl.lag) * K + pl.S);
+        while (issued < lim) {
+          const int64_t r = issued / K;
+          fwd_issue_chunk<X, RT>(p, pl, L, smem, cid + r * ncl, static_cast<int>(issued - r * K),
+                                 static_cast<int>(issued % pl.S), slice_elt0, pol);
+          ++issued;
+        }
+      }
+    }
+    failed = __syncthreads_or(failed);
+    if (failed && tid == 0) drain_ring(pl, L, i * K, issued);
+    return;
   }
 
   const int xs_stride = static_cast<int>(pl.row_bytes[0] / sizeof(X));  // elements per staged row
@@ -347,6 +509,29 @@ __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& 
     bulk_load(st + pl.off[2], static_cast<const DROT*>(p.dro) + e0, b2, &L.full[s], pol);
 }
 
+// Split-row pipeline: sub-chunk j of the row slice of tile `tile` into ring slot `slot`;
+// sub-chunk 0 also brings the row's rstd.
+template <typename X, typename DY, typename DROT>
+__device__ __forceinline__ void bwd_issue_chunk(const BwdParams& p, const StreamPlan& pl, const SmemLayout& L,
+                                                unsigned char* smem, int64_t tile, int j, int slot,
+                                                int64_t slice_elt0, uint64_t pol) {
+  unsigned char* st = smem + static_cast<size_t>(slot) * pl.stage_bytes;
+  fence_proxy_async_smem();
+  if (j == 0) {
+    cp_async_4(st + pl.off[3], p.rstd + tile);
+    cp_async_arrive(&L.full[slot]);
+  }
+  const uint32_t b0 = pl.row_bytes[0];
+  const uint32_t b1 = pl.row_bytes[1];
+  const uint32_t b2 = Present<DROT>::value ? pl.row_bytes[2] : 0u;
+  mbar_arrive_expect_tx(&L.full[slot], b0 + b1 + b2);
+  const int64_t e0 = tile * pl.W + slice_elt0 + static_cast<int64_t>(j) * (pl.vslice / pl.K) * 8;
+  bulk_load(st + pl.off[0], static_cast<const X*>(p.x) + e0, b0, &L.full[slot], pol);
+  bulk_load(st + pl.off[1], static_cast<const DY*>(p.dy) + e0, b1, &L.full[slot], pol);
+  if constexpr (Present<DROT>::value)
+    bulk_load(st + pl.off[2], static_cast<const DROT*>(p.dro) + e0, b2, &L.full[slot], pol);
+}
+
 // X: saved input dtype; DY: dout dtype; DXT: dx dtype; DROT: dresidual_out dtype (NoT =
 // none); DREST: dresidual dtype (NoT = not written).
 template <typename X, typename DY, typename DXT, typename DROT, typename DREST, bool kHasDb, int kVecs,
@@ -374,7 +559,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   const int rstd_per_row = pl.seg_mode ? pl.heads : 1;
   const uint64_t pol = l2_policy_evict_first();
   int64_t issued = 0;
-  if (tid == 0) {
+  if (tid == 0 && pl.P == 1) {
     for (int j = 0; j < pl.S; ++j) {
       const int64_t t = cid + j * ncl;
       if (t >= pl.ntiles) break;
@@ -409,10 +594,112 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     if (((vmask >> k) & 1u) && p.w != nullptr) load8_rt(p.w, p.w_dt, p.w_per_head ? c : c % pl.N, wr[k], true);
   }
 
+  bool failed = false;
+  int64_t i = 0;
+  if (pl.P > 1) {
+    // ------------- split-row pipeline (row slices across a cluster, R = 1) -------------
+    // As in the forward: K sub-chunks per row slice through an S-slot ring; pass 1 of row
+    // i (dot product, dweight/dbias accumulation) overlaps the cluster exchange of row
+    // i-1, whose pass 2 (dx) follows.
+    const int K = pl.K;
+    const int kpc_mask = (1 << pl.kpc_shift) - 1;
+    const int64_t n_local = cid < pl.ntiles ? (pl.ntiles - 1 - cid) / ncl + 1 : 0;
+    const int64_t total_q = n_local * K;
+    const bool grp = tid < G;
+    auto issue_upto = [&](int64_t lim) {
+      while (issued < lim) {
+        const int64_t r = issued / K;
+        bwd_issue_chunk<X, DY, DROT>(p, pl, L, smem, cid + r * ncl, static_cast<int>(issued - r * K),
+                                     static_cast<int>(issued % pl.S), slice_elt0, pol);
+        ++issued;
+      }
+    };
+    if (tid == 0) issue_upto(min(total_q, static_cast<int64_t>(pl.S)));
+    auto slot_base = [&](int64_t row_local, int k) -> const unsigned char* {
+      const int64_t q = row_local * K + (k >> pl.kpc_shift);
+      return smem + static_cast<size_t>(q % pl.S) * pl.stage_bytes;
+    };
+    auto row_rstd = [&](int64_t row_local) -> float {
+      return *reinterpret_cast<const float*>(slot_base(row_local, 0) + pl.off[3]);
+    };
+    for (; i < n_local + pl.lag; ++i) {
+      bool ok = true;
+      if (i < n_local) {
+        for (int j = 0; j < K; ++j) {
+          const int64_t q = i * K + j;
+          ok = mbar_wait(&L.full[q % pl.S], static_cast<uint32_t>(q / pl.S) & 1u, kSiteBwdFull) && ok;
+        }
+      }
+      if (__syncthreads_or(!ok || failed)) { failed = true; break; }
+      if (grp) {
+        if (i < n_local) {
+          const float r = row_rstd(i);
+          float dot = 0.f;
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) {
+            if ((vmask >> k) & 1u) {
+              const int off = (gl + (k & kpc_mask) * G) * 8;
+              const unsigned char* sb = slot_base(i, k);
+              float xv[8], dv[8];
+              Vec8<X>::load(reinterpret_cast<const X*>(sb + pl.off[0]) + off, xv);
+              Vec8<DY>::load(reinterpret_cast<const DY*>(sb + pl.off[1]) + off, dv);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float xh = xv[e] * r;
+                dot = fmaf(xh, dv[e] * wr[k][e], dot);
+                dw[k][e] = fmaf(dv[e], xh, dw[k][e]);
+                if constexpr (kHasDb) db[kHasDb ? k : 0][e] += dv[e];
+              }
+            }
+          }
+          dot = group_sum(dot, pl, L, 0, gl, static_cast<uint32_t>(i));
+          cluster_send(dot, pl, L, gl, static_cast<uint32_t>(i), rank);
+        }
+        const int64_t r2 = i - pl.lag;
+        if (r2 >= 0 && r2 < n_local) {
+          float tot;
+          if (!cluster_recv(tot, pl, L, 0, gl, static_cast<uint32_t>(r2), kSiteBwdCluster)) {
+            failed = true;
+          } else {
+            const float c = tot / n_f;
+            const float r = row_rstd(r2);
+            const int64_t g0 = (cid + r2 * ncl) * pl.W + slice_elt0 + gl * 8;
+            DXT* dxp = static_cast<DXT*>(p.dx) + g0;
+            DRESe* drp = static_cast<DRESe*>(p.dres) + g0;
+#pragma unroll
+            for (int k = 0; k < kVecs; ++k) {
+              if ((vmask >> k) & 1u) {
+                const int off = (gl + (k & kpc_mask) * G) * 8;
+                const unsigned char* sb = slot_base(r2, k);
+                float xv[8], dv[8], g[8];
+                Vec8<X>::load(reinterpret_cast<const X*>(sb + pl.off[0]) + off, xv);
+                Vec8<DY>::load(reinterpret_cast<const DY*>(sb + pl.off[1]) + off, dv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) g[e] = (dv[e] * wr[k][e] - (xv[e] * r) * c) * r;
+                if constexpr (kDro) {
+                  float a[8];
+                  Vec8<DROe>::load(reinterpret_cast<const DROe*>(sb + pl.off[2]) + off, a);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) g[e] += a[e];
+                }
+                Vec8<DXT>::store(dxp + k * G8, g);
+                if constexpr (kDres) Vec8<DRESe>::store(drp + k * G8, g);
+              }
+            }
+          }
+        }
+      }
+      __syncthreads();  // pass 2 of row i - lag is done: its slots are free
+      if (tid == 0) issue_upto(min(total_q, max(static_cast<int64_t>(0), i + 1 - pl.lag) * K + pl.S));
+    }
+    failed = __syncthreads_or(failed);
+    if (failed) {
+      if (tid == 0) drain_ring(pl, L, i * K, issued);
+      return;
+    }
+  } else {
   const int x_stride = static_cast<int>(pl.row_bytes[0] / sizeof(X));
   uint32_t seq = 0;
-  int64_t i = 0;
-  bool failed = false;
   for (int64_t tile = cid; tile < pl.ntiles; tile += ncl, ++i) {
     const int s = static_cast<int>(i % pl.S);
     const bool ok = mbar_wait(&L.full[s], static_cast<uint32_t>(i / pl.S) & 1u, kSiteBwdFull);
@@ -519,6 +806,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     if (tid == 0) drain_ring(pl, L, i, issued);
     return;
   }
+  }  // tile loop
 
   // one partial row per (cluster, row group): the groups of a CTA own the same columns.
   // Every owned column is written, zeros included, so the reduction reads no stale data.
