@@ -337,6 +337,56 @@ def run_reference_arm(args, w):
     print(json.dumps(line), flush=True)
 
 
+def run_refgpu(args, w):
+    """Times the reference's Hopper kernels (recompiled for sm_100a) on this workload, one
+    GPU, device time of K steps (CUDA graph replay when capturable, else eager)."""
+    from oracle import ref_gpu
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ext = ref_gpu.load()
+    h = w.get("heads", 1)
+    one_set = algo_bytes(w)
+    pool = 1 if one_set > 2 * L2_BYTES else max(2, -(-3 * L2_BYTES // one_set))
+    sets = [make_inputs(w, dev, 100 * i) for i in range(pool)]
+    steps = [ref_gpu.make_step(ext, w["kind"], t, heads=h, ro_dtype=w.get("ro"), store_rstd=w.get("rstd", False),
+                               has_bias=w.get("bias", False) if w["kind"] == "bwd" else False) for t in sets]
+    for i in range(args.warmup):
+        steps[i % pool]()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    graph, how = None, "eager launches"
+    try:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for i in range(args.steps):
+                steps[i % pool]()
+        stream.wait_stream(side)
+        g.replay()
+        torch.cuda.synchronize(dev)
+        graph, how = g, "CUDA graph replay of the K steps"
+    except Exception as exc:  # the reference's bindings allocate and cache per call
+        log(f"[bench] reference steps not capturable ({exc}); timing eager launches")
+        torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    if graph is not None:
+        graph.replay()
+    else:
+        for i in range(args.steps):
+            steps[i % pool]()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / args.steps
+    print(json.dumps({"impl": "refgpu", "metric": METRIC, "value": round(algo_bytes(w) / (ms * 1e-3) / 1e9, 2),
+                      "unit": "GB/s", "ms_per_step": round(ms, 5), "n_gpus": 1, "steps": args.steps,
+                      "warmup": args.warmup, "config": {"workload": w["desc"], "timing": how,
+                      "kernels": "reference rmsnorm/csrc recompiled for sm_100a (oracle/_ref)"}}), flush=True)
+
+
 def e2e_measure(w, t_dev, dev, steps, group):
     """Public API with pinned host buffers (rmsnorm.host_pipeline.HostPipeline): every step
     copies its inputs host->device, runs the kernels, and copies its results back, with
@@ -416,7 +466,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "refgpu"], default="ours",
+                    help="refgpu: the reference's own CUDA kernels recompiled for sm_100a (oracle/_ref), "
+                         "timed on the same workload for comparison")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -432,6 +484,9 @@ def main():
 
     if args.impl == "reference":
         run_reference_arm(args, w)
+        return
+    if args.impl == "refgpu":
+        run_refgpu(args, w)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

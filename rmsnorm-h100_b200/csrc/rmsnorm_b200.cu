@@ -229,11 +229,14 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
       for (int t = 0; t < 3; ++t) chunk = align_up(chunk + static_cast<uint32_t>(pl.vslice / k) * 8u * in_bytes[t], 128);
       if (rstd_staged) chunk += 128;
       const int s_max = std::min<int>(kMaxStages, budget / static_cast<int>(chunk));
+      if (k > 1 && chunk < 32 * 1024 && !force_k) continue;  // small bulk copies stream poorly
       for (int lag = 1; lag >= 0; --lag) {
         if (force_lag >= 0 && lag != force_lag) continue;
         if (s_max < (1 + lag) * k) continue;
         const int64_t inflight = static_cast<int64_t>(s_max - (1 + lag) * k) * chunk;
-        const int64_t score = inflight + ((lag == 1 && inflight >= 64 * 1024) ? (int64_t(1) << 40) : 0);
+        // lag 1 only when at least two sub-chunks (>= 64 KB) stay in flight behind it
+        const int64_t score = inflight + ((lag == 1 && inflight >= 64 * 1024 && s_max - 2 * k >= 2)
+                                              ? (int64_t(1) << 40) : 0);
         if (score > best_score) {
           best_score = score;
           best_k = k;
@@ -607,7 +610,7 @@ int plan_bwd(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdPlan* bp) {
     if (have_small && have_large) {
       const int64_t sms_large = static_cast<int64_t>(cand_large.grid);
       const int64_t sms_small = static_cast<int64_t>(cand_small.grid) / kSmall.ctas_per_sm;
-      if (sms_small < sms_large) have_small = false;
+      if (sms_small <= sms_large) have_small = false;
     }
     if (have_small) { *bp = cand_small; return RMSNORM_B200_OK; }
     if (have_large) { *bp = cand_large; return RMSNORM_B200_OK; }

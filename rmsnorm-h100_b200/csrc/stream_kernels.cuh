@@ -264,50 +264,56 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
     // pass 1 of row i and posts its partial sum to the cluster, then (lag 1) receives
     // row i-1's total and runs its pass 2, so the exchange overlaps a whole pass 1.
     const int K = pl.K;
+    const int S = pl.S;
     const int kpc_mask = (1 << pl.kpc_shift) - 1;
     const int64_t n_local = cid < pl.ntiles ? (pl.ntiles - 1 - cid) / ncl + 1 : 0;
     const int64_t total_q = n_local * K;
     const bool grp = tid < G;
-    if (tid == 0) {
-      while (issued < min(total_q, static_cast<int64_t>(pl.S))) {
-        const int64_t r = issued / K;
-        fwd_issue_chunk<X, RT>(p, pl, L, smem, cid + r * ncl, static_cast<int>(issued - r * K),
-                               static_cast<int>(issued % pl.S), slice_elt0, pol);
+    // ring positions are tracked incrementally (no 64-bit division in the loop)
+    int iss_slot = 0, iss_j = 0;
+    int64_t iss_tile = cid;
+    auto issue_upto = [&](int64_t lim) {
+      while (issued < lim) {
+        fwd_issue_chunk<X, RT>(p, pl, L, smem, iss_tile, iss_j, iss_slot, slice_elt0, pol);
         ++issued;
+        if (++iss_slot == S) iss_slot = 0;
+        if (++iss_j == K) { iss_j = 0; iss_tile += ncl; }
       }
-    }
-    auto xptr = [&](int64_t row_local, int k) -> const X* {
-      const int64_t q = row_local * K + (k >> pl.kpc_shift);
-      return reinterpret_cast<const X*>(smem + static_cast<size_t>(q % pl.S) * pl.stage_bytes + pl.off[0]) +
-             (gl + (k & kpc_mask) * G) * 8;
     };
-    auto rptr = [&](int64_t row_local, int k) -> const RTe* {
-      const int64_t q = row_local * K + (k >> pl.kpc_shift);
-      return reinterpret_cast<const RTe*>(smem + static_cast<size_t>(q % pl.S) * pl.stage_bytes + pl.off[1]) +
-             (gl + (k & kpc_mask) * G) * 8;
+    if (tid == 0) issue_upto(min(total_q, static_cast<int64_t>(S)));
+    auto slot_ptr = [&](int base, int k, uint32_t off) -> const unsigned char* {
+      int sl = base + (k >> pl.kpc_shift);
+      if (sl >= S) sl -= S;
+      return smem + static_cast<size_t>(sl) * pl.stage_bytes + off;
     };
+    int row_slot = 0;       // ring slot of sub-chunk 0 of row i
+    uint32_t row_phase = 0;  // its mbarrier phase parity
     bool failed = false;
     int64_t i = 0;
     for (; i < n_local + pl.lag; ++i) {
       bool ok = true;
       if (i < n_local) {
         for (int j = 0; j < K; ++j) {
-          const int64_t q = i * K + j;
-          ok = mbar_wait(&L.full[q % pl.S], static_cast<uint32_t>(q / pl.S) & 1u, kSiteFwdFull) && ok;
+          int sl = row_slot + j;
+          uint32_t ph = row_phase;
+          if (sl >= S) { sl -= S; ph ^= 1u; }
+          ok = mbar_wait(&L.full[sl], ph, kSiteFwdFull) && ok;
         }
       }
       if (__syncthreads_or(!ok || failed)) { failed = true; break; }
       if (grp) {
+        const int xo = gl * 8;
         if (i < n_local) {
           float ss = 0.f;
 #pragma unroll
           for (int k = 0; k < kVecs; ++k) {
             if ((vmask >> k) & 1u) {
+              const int vo = xo + (k & kpc_mask) * G8;
               float h[8];
-              Vec8<X>::load(xptr(i, k), h);
+              Vec8<X>::load(reinterpret_cast<const X*>(slot_ptr(row_slot, k, pl.off[0])) + vo, h);
               if constexpr (kRes) {
                 float r[8];
-                Vec8<RTe>::load(rptr(i, k), r);
+                Vec8<RTe>::load(reinterpret_cast<const RTe*>(slot_ptr(row_slot, k, pl.off[1])) + vo, r);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) h[e] += r[e];
               }
@@ -320,23 +326,26 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
         }
         const int64_t r2 = i - pl.lag;
         if (r2 >= 0 && r2 < n_local) {
+          int base2 = row_slot - pl.lag * K;
+          if (base2 < 0) base2 += S;
           float tot;
           if (!cluster_recv(tot, pl, L, 0, gl, static_cast<uint32_t>(r2), kSiteFwdCluster)) {
             failed = true;
           } else {
             const float rs = rsqrtf(tot / n_f + p.eps);
             const int64_t row = cid + r2 * ncl;
-            const int64_t g0 = row * pl.W + slice_elt0 + gl * 8;
+            const int64_t g0 = row * pl.W + slice_elt0 + xo;
             OT* op = static_cast<OT*>(p.out) + g0;
             ROe* rop = static_cast<ROe*>(p.ro) + g0;
 #pragma unroll
             for (int k = 0; k < kVecs; ++k) {
               if ((vmask >> k) & 1u) {
+                const int vo = xo + (k & kpc_mask) * G8;
                 float h[8];
-                Vec8<X>::load(xptr(r2, k), h);
+                Vec8<X>::load(reinterpret_cast<const X*>(slot_ptr(base2, k, pl.off[0])) + vo, h);
                 if constexpr (kRes) {
                   float r[8];
-                  Vec8<RTe>::load(rptr(r2, k), r);
+                  Vec8<RTe>::load(reinterpret_cast<const RTe*>(slot_ptr(base2, k, pl.off[1])) + vo, r);
 #pragma unroll
                   for (int e = 0; e < 8; ++e) h[e] += r[e];
                 }
@@ -352,14 +361,10 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
         }
       }
       __syncthreads();  // pass 2 of row i - lag is done: its slots are free
-      if (tid == 0) {
-        const int64_t lim = min(total_q, max(static_cast<int64_t>(0), i + 1 - pl.lag) * K + pl.S);
-        while (issued < lim) {
-          const int64_t r = issued / K;
-          fwd_issue_chunk<X, RT>(p, pl, L, smem, cid + r * ncl, static_cast<int>(issued - r * K),
-                                 static_cast<int>(issued % pl.S), slice_elt0, pol);
-          ++issued;
-        }
+      if (tid == 0) issue_upto(min(total_q, max(static_cast<int64_t>(0), i + 1 - pl.lag) * K + S));
+      if (i < n_local) {
+        row_slot += K;
+        if (row_slot >= S) { row_slot -= S; row_phase ^= 1u; }
       }
     }
     failed = __syncthreads_or(failed);
@@ -602,47 +607,53 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     // i (dot product, dweight/dbias accumulation) overlaps the cluster exchange of row
     // i-1, whose pass 2 (dx) follows.
     const int K = pl.K;
+    const int S = pl.S;
     const int kpc_mask = (1 << pl.kpc_shift) - 1;
     const int64_t n_local = cid < pl.ntiles ? (pl.ntiles - 1 - cid) / ncl + 1 : 0;
     const int64_t total_q = n_local * K;
     const bool grp = tid < G;
+    int iss_slot = 0, iss_j = 0;
+    int64_t iss_tile = cid;
     auto issue_upto = [&](int64_t lim) {
       while (issued < lim) {
-        const int64_t r = issued / K;
-        bwd_issue_chunk<X, DY, DROT>(p, pl, L, smem, cid + r * ncl, static_cast<int>(issued - r * K),
-                                     static_cast<int>(issued % pl.S), slice_elt0, pol);
+        bwd_issue_chunk<X, DY, DROT>(p, pl, L, smem, iss_tile, iss_j, iss_slot, slice_elt0, pol);
         ++issued;
+        if (++iss_slot == S) iss_slot = 0;
+        if (++iss_j == K) { iss_j = 0; iss_tile += ncl; }
       }
     };
-    if (tid == 0) issue_upto(min(total_q, static_cast<int64_t>(pl.S)));
-    auto slot_base = [&](int64_t row_local, int k) -> const unsigned char* {
-      const int64_t q = row_local * K + (k >> pl.kpc_shift);
-      return smem + static_cast<size_t>(q % pl.S) * pl.stage_bytes;
+    if (tid == 0) issue_upto(min(total_q, static_cast<int64_t>(S)));
+    auto slot_base = [&](int base, int k) -> const unsigned char* {
+      int sl = base + (k >> pl.kpc_shift);
+      if (sl >= S) sl -= S;
+      return smem + static_cast<size_t>(sl) * pl.stage_bytes;
     };
-    auto row_rstd = [&](int64_t row_local) -> float {
-      return *reinterpret_cast<const float*>(slot_base(row_local, 0) + pl.off[3]);
-    };
+    int row_slot = 0;
+    uint32_t row_phase = 0;
     for (; i < n_local + pl.lag; ++i) {
       bool ok = true;
       if (i < n_local) {
         for (int j = 0; j < K; ++j) {
-          const int64_t q = i * K + j;
-          ok = mbar_wait(&L.full[q % pl.S], static_cast<uint32_t>(q / pl.S) & 1u, kSiteBwdFull) && ok;
+          int sl = row_slot + j;
+          uint32_t ph = row_phase;
+          if (sl >= S) { sl -= S; ph ^= 1u; }
+          ok = mbar_wait(&L.full[sl], ph, kSiteBwdFull) && ok;
         }
       }
       if (__syncthreads_or(!ok || failed)) { failed = true; break; }
       if (grp) {
+        const int xo = gl * 8;
         if (i < n_local) {
-          const float r = row_rstd(i);
+          const float r = *reinterpret_cast<const float*>(slot_base(row_slot, 0) + pl.off[3]);
           float dot = 0.f;
 #pragma unroll
           for (int k = 0; k < kVecs; ++k) {
             if ((vmask >> k) & 1u) {
-              const int off = (gl + (k & kpc_mask) * G) * 8;
-              const unsigned char* sb = slot_base(i, k);
+              const int vo = xo + (k & kpc_mask) * G8;
+              const unsigned char* sb = slot_base(row_slot, k);
               float xv[8], dv[8];
-              Vec8<X>::load(reinterpret_cast<const X*>(sb + pl.off[0]) + off, xv);
-              Vec8<DY>::load(reinterpret_cast<const DY*>(sb + pl.off[1]) + off, dv);
+              Vec8<X>::load(reinterpret_cast<const X*>(sb + pl.off[0]) + vo, xv);
+              Vec8<DY>::load(reinterpret_cast<const DY*>(sb + pl.off[1]) + vo, dv);
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 const float xh = xv[e] * r;
@@ -657,28 +668,30 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
         }
         const int64_t r2 = i - pl.lag;
         if (r2 >= 0 && r2 < n_local) {
+          int base2 = row_slot - pl.lag * K;
+          if (base2 < 0) base2 += S;
           float tot;
           if (!cluster_recv(tot, pl, L, 0, gl, static_cast<uint32_t>(r2), kSiteBwdCluster)) {
             failed = true;
           } else {
             const float c = tot / n_f;
-            const float r = row_rstd(r2);
-            const int64_t g0 = (cid + r2 * ncl) * pl.W + slice_elt0 + gl * 8;
+            const float r = *reinterpret_cast<const float*>(slot_base(base2, 0) + pl.off[3]);
+            const int64_t g0 = (cid + r2 * ncl) * pl.W + slice_elt0 + xo;
             DXT* dxp = static_cast<DXT*>(p.dx) + g0;
             DRESe* drp = static_cast<DRESe*>(p.dres) + g0;
 #pragma unroll
             for (int k = 0; k < kVecs; ++k) {
               if ((vmask >> k) & 1u) {
-                const int off = (gl + (k & kpc_mask) * G) * 8;
-                const unsigned char* sb = slot_base(r2, k);
+                const int vo = xo + (k & kpc_mask) * G8;
+                const unsigned char* sb = slot_base(base2, k);
                 float xv[8], dv[8], g[8];
-                Vec8<X>::load(reinterpret_cast<const X*>(sb + pl.off[0]) + off, xv);
-                Vec8<DY>::load(reinterpret_cast<const DY*>(sb + pl.off[1]) + off, dv);
+                Vec8<X>::load(reinterpret_cast<const X*>(sb + pl.off[0]) + vo, xv);
+                Vec8<DY>::load(reinterpret_cast<const DY*>(sb + pl.off[1]) + vo, dv);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) g[e] = (dv[e] * wr[k][e] - (xv[e] * r) * c) * r;
                 if constexpr (kDro) {
                   float a[8];
-                  Vec8<DROe>::load(reinterpret_cast<const DROe*>(sb + pl.off[2]) + off, a);
+                  Vec8<DROe>::load(reinterpret_cast<const DROe*>(sb + pl.off[2]) + vo, a);
 #pragma unroll
                   for (int e = 0; e < 8; ++e) g[e] += a[e];
                 }
@@ -690,7 +703,11 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
         }
       }
       __syncthreads();  // pass 2 of row i - lag is done: its slots are free
-      if (tid == 0) issue_upto(min(total_q, max(static_cast<int64_t>(0), i + 1 - pl.lag) * K + pl.S));
+      if (tid == 0) issue_upto(min(total_q, max(static_cast<int64_t>(0), i + 1 - pl.lag) * K + S));
+      if (i < n_local) {
+        row_slot += K;
+        if (row_slot >= S) { row_slot -= S; row_phase ^= 1u; }
+      }
     }
     failed = __syncthreads_or(failed);
     if (failed) {
