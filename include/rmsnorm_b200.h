@@ -64,7 +64,8 @@ enum {
   RMSNORM_B200_ERR_WORKSPACE = 3,
   RMSNORM_B200_ERR_CUDA = 4,
   RMSNORM_B200_ERR_DEVICE_TIMEOUT = 5,
-  RMSNORM_B200_ERR_NO_DEVICE = 6
+  RMSNORM_B200_ERR_NO_DEVICE = 6,
+  RMSNORM_B200_ERR_SCRATCH_LIMIT = 7
 };
 
 /* Forward arguments. Pointers marked nullable may be NULL. All row-major, contiguous. */
@@ -132,6 +133,27 @@ int rmsnorm_b200_bwd_workspace_size(const rmsnorm_b200_bwd_args* args, size_t* b
  * ignored and it may be reused as soon as the stream has passed this call. */
 int rmsnorm_b200_bwd(const rmsnorm_b200_bwd_args* args, void* workspace, size_t workspace_bytes,
                      void* stream);
+
+/* Backward that allocates nothing: the same kernels as rmsnorm_b200_bwd, with the
+ * dweight/dbias partial sums kept in a scratch buffer built into the library instead of a
+ * caller-provided workspace. No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory at call time: a plugin inside a host
+ * framework that has reserved all device memory for its own pool, or code that must not
+ * allocate once it is running (allocation can block, fail, or synchronise the device).
+ *
+ * The buffer is RMSNORM_B200_NOALLOC_SCRATCH_BYTES of device memory, one per device,
+ * reserved by every GPU that loads the library until the process exits. Problems whose
+ * partial sums need more return RMSNORM_B200_ERR_SCRATCH_LIMIT without running (every
+ * streaming-kernel problem fits on a B200; only very wide rows on the generic path can
+ * exceed it). The first call on a device looks up the buffer's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture. All calls on a
+ * device share the one buffer, so calls whose kernels overlap on the GPU (different
+ * streams, no ordering between them) race and give wrong dweight/dbias; calls ordered on
+ * one stream are fine. Nothing in the buffer needs to be zero between calls: every
+ * partial sum is written before it is read. */
+#define RMSNORM_B200_NOALLOC_SCRATCH_BYTES (16u << 20)
+int rmsnorm_b200_bwd_noalloc(const rmsnorm_b200_bwd_args* args, void* stream);
 
 /* Static, human-readable message for a status code. */
 const char* rmsnorm_b200_strerror(int status);

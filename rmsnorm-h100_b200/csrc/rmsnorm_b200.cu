@@ -55,6 +55,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // ------------------------------------------------------------------------------------
 struct DeviceState {
   int sm_count = 0;
+  void* noalloc_scratch = nullptr;  // device address of g_noalloc_scratch on this device
   std::mutex mu;
   std::map<const void*, bool> attrs_done;
   std::map<std::tuple<const void*, int, int, int>, int> occupancy;  // (kernel, P, smem, threads)
@@ -75,6 +76,25 @@ int get_device_state(DeviceState** out) {
     g_devices[dev] = std::move(st);
   }
   *out = g_devices[dev].get();
+  return RMSNORM_B200_OK;
+}
+
+// Scratch for rmsnorm_b200_bwd_noalloc: a file-scope device array, one per device that
+// loads the library. In host code `g_noalloc_scratch` only names a host-side stand-in, so
+// its device address is looked up (per device, with that device current) and passed on.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[RMSNORM_B200_NOALLOC_SCRATCH_BYTES];
+
+int noalloc_scratch(DeviceState* ds, void** out) {
+  std::lock_guard<std::mutex> lock(ds->mu);
+  if (!ds->noalloc_scratch) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) {
+      cudaGetLastError();
+      return RMSNORM_B200_ERR_CUDA;
+    }
+    ds->noalloc_scratch = ptr;
+  }
+  *out = ds->noalloc_scratch;
   return RMSNORM_B200_OK;
 }
 
@@ -736,6 +756,22 @@ extern "C" int rmsnorm_b200_bwd(const rmsnorm_b200_bwd_args* args, void* workspa
   return do_bwd(args, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int rmsnorm_b200_bwd_noalloc(const rmsnorm_b200_bwd_args* args, void* stream) {
+  int st = check_bwd(args);
+  if (st) return st;
+  DeviceState* ds = nullptr;
+  st = get_device_state(&ds);
+  if (st) return st;
+  void* scratch = nullptr;
+  st = noalloc_scratch(ds, &scratch);
+  if (st) return st;
+  BwdPlan bp;
+  st = plan_bwd(ds, args, &bp);
+  if (st) return st;
+  if (workspace_for(bp) > RMSNORM_B200_NOALLOC_SCRATCH_BYTES) return RMSNORM_B200_ERR_SCRATCH_LIMIT;
+  return do_bwd(args, scratch, RMSNORM_B200_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" const char* rmsnorm_b200_strerror(int status) {
   switch (status) {
     case RMSNORM_B200_OK: return "ok";
@@ -745,6 +781,8 @@ extern "C" const char* rmsnorm_b200_strerror(int status) {
     case RMSNORM_B200_ERR_CUDA: return "CUDA launch or runtime error";
     case RMSNORM_B200_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
     case RMSNORM_B200_ERR_NO_DEVICE: return "no CUDA device";
+    case RMSNORM_B200_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the library's built-in no-allocation buffer holds";
     default: return "unknown status";
   }
 }

@@ -24,6 +24,7 @@ _DTYPE_CODES = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}
 
 OK = 0
 ERR_DEVICE_TIMEOUT = 5
+ERR_SCRATCH_LIMIT = 7
 
 
 class FwdArgs(ctypes.Structure):
@@ -91,6 +92,7 @@ SIGNATURES = {
         ctypes.c_int,
         [ctypes.POINTER(BwdArgs), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p],
     ),
+    "rmsnorm_b200_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(BwdArgs), ctypes.c_void_p]),
     "rmsnorm_b200_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "rmsnorm_b200_device_status": (
         ctypes.c_int,
@@ -275,6 +277,13 @@ def bwd(a: BwdArgs, device: torch.device, workspace: Optional[torch.Tensor] = No
             lib.rmsnorm_b200_bwd(ctypes.byref(a), ws_ptr, nbytes, _stream_handle(device)),
             "rmsnorm_b200_bwd",
         )
+
+
+def bwd_noalloc(a: BwdArgs, device: torch.device) -> int:
+    """Backward through the entry point that allocates nothing (the library's built-in
+    scratch buffer replaces the workspace). Returns the status code."""
+    with torch.cuda.device(device):
+        return int(load_library().rmsnorm_b200_bwd_noalloc(ctypes.byref(a), _stream_handle(device)))
 
 
 def device_status(device: torch.device, clear: bool = False) -> tuple:
