@@ -115,10 +115,10 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 }
 
 // Bounded wait, slow path: returns false (after recording the error) when the phase has
-// not completed within g_wait_timeout_ns, or as soon as another thread of any CTA has
-// recorded an error.
+// not completed within g_wait_timeout_ns, or -- when `honor_abort` -- as soon as another
+// thread of any CTA has recorded an error.
 template <bool kClusterScope>
-__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int where) {
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int where, bool honor_abort) {
   const uint64_t t0 = globaltimer_ns();
   const uint64_t limit = g_wait_timeout_ns;
   uint32_t spins = 0;
@@ -127,7 +127,7 @@ __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int 
       return true;
     }
     if ((++spins & 15u) == 0u) {
-      if (abort_requested()) return false;
+      if (honor_abort && abort_requested()) return false;
       if (globaltimer_ns() - t0 > limit) {
         record_error(RMSNORM_B200_ERR_DEVICE_TIMEOUT, where);
         return false;
@@ -138,9 +138,9 @@ __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int 
 
 // Bounded wait: one inline probe, then the out-of-line bounded loop.
 template <bool kClusterScope = false>
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int where) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int where, bool honor_abort = true) {
   if (kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
-  return mbar_wait_slow<kClusterScope>(bar, parity, where);
+  return mbar_wait_slow<kClusterScope>(bar, parity, where, honor_abort);
 }
 
 // ---------------------------------------------------------------------------------------

@@ -228,59 +228,27 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
   pl.P = P;
   pl.rps = P > 1 ? 1 : T / pl.G;
   if (pl.rps < 1) { *why = "group wider than the CTA"; return false; }
-  pl.K = 1;
   pl.lag = 0;
-  pl.kpc_shift = log2i(max_vecs);
 
   if (P > 1) {
-    // Split-row pipeline: pick sub-chunks per slice K and the exchange lag that keep the
-    // most bytes loading while rows wait. Lag 1 keeps two rows resident (S >= 2K), lag 0
-    // one (S >= K); K > 1 needs every thread to own max_vecs vectors of the slice.
-    const bool full = pl.vslice == pl.G * max_vecs;
-    const int force_k = env_int("RMSNORM_B200_FORCE_K", 0);
-    const int force_lag = env_int("RMSNORM_B200_FORCE_LAG", -1);
-    int best_k = 0, best_lag = 0, best_s = 0;
-    int64_t best_score = -1;
-    uint32_t best_chunk = 0;
-    for (int k = 1; k <= 4 && k <= max_vecs; k <<= 1) {
-      if (max_vecs % k || (k > 1 && !full)) continue;
-      if (force_k && k != force_k) continue;
-      uint32_t chunk = 0;
-      for (int t = 0; t < 3; ++t) chunk = align_up(chunk + static_cast<uint32_t>(pl.vslice / k) * 8u * in_bytes[t], 128);
-      if (rstd_staged) chunk += 128;
-      const int s_max = std::min<int>(kMaxStages, budget / static_cast<int>(chunk));
-      if (k > 1 && chunk < 32 * 1024 && !force_k) continue;  // small bulk copies stream poorly
-      for (int lag = 1; lag >= 0; --lag) {
-        if (force_lag >= 0 && lag != force_lag) continue;
-        if (s_max < (1 + lag) * k) continue;
-        const int64_t inflight = static_cast<int64_t>(s_max - (1 + lag) * k) * chunk;
-        // lag 1 only when at least two sub-chunks (>= 64 KB) stay in flight behind it
-        const int64_t score = inflight + ((lag == 1 && inflight >= 64 * 1024 && s_max - 2 * k >= 2)
-                                              ? (int64_t(1) << 40) : 0);
-        if (score > best_score) {
-          best_score = score;
-          best_k = k;
-          best_lag = lag;
-          best_s = s_max;
-          best_chunk = chunk;
-        }
-      }
-    }
-    if (best_k == 0) { *why = "no split-row ring fits"; return false; }
-    pl.K = best_k;
-    pl.lag = best_lag;
-    pl.kpc_shift = log2i(max_vecs / best_k);
+    // Split-row pipeline: one slot per row slice; lag 1 (pass 2 of row i-1 runs while
+    // row i's exchange is in flight) needs two resident rows, so S >= 2.
     pl.R = 1;
     uint32_t off = 0;
     for (int t = 0; t < 3; ++t) {
-      pl.row_bytes[t] = static_cast<uint32_t>(pl.vslice / best_k) * 8u * in_bytes[t];
+      pl.row_bytes[t] = static_cast<uint32_t>(pl.vslice) * 8u * in_bytes[t];
       pl.off[t] = off;
       off = align_up(off + pl.row_bytes[t], 128);
     }
     pl.off[3] = off;
-    pl.stage_bytes = best_chunk;
+    if (rstd_staged) off += 128;
+    pl.stage_bytes = off;
     const int max_s = std::max(1, std::min(kMaxStages, env_int("RMSNORM_B200_MAX_STAGES", kMaxStages)));
-    pl.S = std::max((1 + best_lag) * best_k, std::min(best_s, max_s));
+    pl.S = std::min<int>(max_s, budget / static_cast<int>(off));
+    if (pl.S < 1) { *why = "no split-row ring fits"; return false; }
+    const int force_lag = env_int("RMSNORM_B200_FORCE_LAG", -1);
+    pl.lag = pl.S >= 2 ? 1 : 0;
+    if (force_lag == 0) pl.lag = 0;
     pl.ntiles = pl.nrows;
     *out = pl;
     return true;
@@ -332,9 +300,9 @@ std::string describe(const char* kind, const StreamPlan& pl, int grid) {
   char buf[512];
   std::snprintf(buf, sizeof(buf),
                 "%s mode=%s P=%d grid=%d clusters=%d T=%d G=%d rps=%d R=%d S=%d stage=%u "
-                "vslice=%d vs=%d K=%d lag=%d tiles=%lld",
+                "vslice=%d vs=%d lag=%d tiles=%lld",
                 kind, pl.seg_mode ? "seg" : "row", pl.P, grid, pl.nclusters, pl.T, pl.G, pl.rps,
-                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, pl.K, pl.lag, static_cast<long long>(pl.ntiles));
+                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, pl.lag, static_cast<long long>(pl.ntiles));
   return buf;
 }
 

@@ -1,27 +1,30 @@
 // stream_kernels.cuh -- the persistent, TMA-staged forward and backward kernels.
 //
 // Structure (both directions):
-//   * one CTA of 512 threads per SM, or two CTAs of 256 threads per SM (launch variant for
-//     rows split across clusters, so that two independent row pipelines share each SM);
-//     persistent over tiles assigned round-robin (tile = cluster id + k * clusters);
-//   * thread 0 streams each tile HBM -> shared memory with cp.async.bulk (one bulk copy
-//     per tensor per tile when P == 1, one per row slice when P > 1) into an S-deep ring of
-//     stages; each stage's "full" mbarrier counts the bytes landing. Right after the
-//     CTA-wide vote that opens tile i, thread 0 refills the stage tile i-1 used with tile
-//     i-1+S, so S-1 tiles are always in flight behind the one being computed;
+//   * one CTA of 512 threads per SM (or 256 threads, two per SM), persistent over tiles
+//     assigned round-robin (local tile q of cluster c is tile c + q * clusters);
+//   * tiles stream HBM -> shared memory with cp.async.bulk (TMA bulk copies, no tensor map,
+//     no multicast; one copy per tensor per tile) into an S-slot ring; each slot's "full"
+//     mbarrier counts the landing bytes. There is no CTA-wide barrier per tile: every warp
+//     waits on the slot's mbarrier, and when it is done with the slot it bumps the slot's
+//     shared-memory counter; the last warp to finish refills the slot with tile q + S;
 //   * threads read 8-element vectors from shared memory, reduce the row (xor shuffles in a
-//     warp, one named barrier + one shared load + a second shuffle tree across the warps of
-//     a row group, st.async + mbarrier exchange through distributed shared memory across
-//     the CTAs of a cluster), then re-read the stage and write outputs with 16-byte
-//     coalesced streaming stores;
+//     warp; one named barrier + one shared load + a second shuffle tree across the warps of
+//     a row group; for rows split over a cluster of P CTAs, warp 0 sends the CTA's total to
+//     every peer in parallel with st.async (lane q -> peer q) and every warp sums the P
+//     totals it receives), then re-read the slot and write outputs with 16-byte coalesced
+//     streaming stores. Split rows are software-pipelined one row deep: pass 1 of row i and
+//     its exchange overlap pass 2 of row i-1;
 //   * every per-element dtype is a template parameter (absent tensors are `NoT`), so the
 //     inner loops carry no runtime type dispatch;
 //   * affine parameters live in registers for the whole kernel (each thread always owns
 //     the same columns), so dweight/dbias accumulate in registers and are written once
 //     per (cluster, row group) as a partial row; a second kernel sums the partials in a
 //     fixed order.
-// Every wait is bounded; a wait that gives up records an error in the device status word
-// and the CTA leaves its loop at the next CTA-wide vote (after its in-flight copies land).
+// Every wait is bounded. A wait that gives up records an error in the device status word;
+// from then on every wait of every CTA returns at once, so the kernel runs to its end on
+// the same control flow (results undefined, status reported), lets its in-flight copies
+// land, and exits.
 #pragma once
 
 #include <type_traits>
@@ -31,15 +34,14 @@
 
 namespace rmsb200 {
 
-constexpr int kXSlots = 4;  // cluster exchange slots (sequence number mod 4)
+constexpr int kXSlots = 4;  // cluster exchange slots (row sequence number mod 4)
 
 struct SmemLayout {
-  uint64_t* full;   // [kMaxStages]
+  uint64_t* full;   // [kMaxStages] slot filled
   uint64_t* xbar;   // [kXSlots] cluster exchange barriers
-  float* xpart;     // [kXSlots][kMaxCluster] partial sums received from the cluster
+  float* xpart;     // [kXSlots][kMaxCluster] row totals of the cluster's CTAs
   float* red;       // [2][32] per-warp partials (double buffered)
-  float* bc;        // [kXSlots] cluster total broadcast to the row group
-  int* bcf;         // [kXSlots] ... and whether the exchange completed
+  int* done;        // [kMaxStages] warps finished with the slot's current tile
 };
 
 __device__ __forceinline__ SmemLayout carve_smem(unsigned char* smem, const StreamPlan& pl) {
@@ -49,19 +51,37 @@ __device__ __forceinline__ SmemLayout carve_smem(unsigned char* smem, const Stre
   L.xbar = L.full + kMaxStages;
   L.xpart = reinterpret_cast<float*>(L.xbar + kXSlots);
   L.red = L.xpart + kXSlots * kMaxCluster;
-  L.bc = L.red + 64;
-  L.bcf = reinterpret_cast<int*>(L.bc + kXSlots);
+  L.done = reinterpret_cast<int*>(L.red + 64);
   return L;
 }
 
 __device__ __forceinline__ void init_barriers(const SmemLayout& L, const StreamPlan& pl) {
   if (threadIdx.x == 0) {
-    for (int s = 0; s < pl.S; ++s) mbar_init(&L.full[s], 1);
+    for (int s = 0; s < pl.S; ++s) {
+      mbar_init(&L.full[s], 1);
+      L.done[s] = 0;
+    }
     for (int s = 0; s < kXSlots; ++s) mbar_init(&L.xbar[s], 1);
     fence_mbar_init();
   }
   __syncthreads();
   if (pl.P > 1) cluster_sync_all();
+}
+
+// Called by every lane of a warp after its last read of slot s. Returns true on lane 0 of
+// the warp that finishes the slot last; that lane refills it.
+__device__ __forceinline__ bool release_slot(const SmemLayout& L, int s, int nwarps) {
+  __syncwarp();
+  bool last = false;
+  if ((threadIdx.x & 31) == 0) {
+    __threadfence_block();
+    if (atomicAdd(&L.done[s], 1) == nwarps - 1) {
+      L.done[s] = 0;  // no warp can finish the slot's next tile before it is issued below
+      __threadfence_block();
+      last = true;
+    }
+  }
+  return last;
 }
 
 // Sum of `v` over the G threads of row group `gid` (G a multiple of 32). Every thread of
@@ -81,71 +101,34 @@ __device__ __forceinline__ float group_sum(float v, const StreamPlan& pl, const 
   return v;
 }
 
-// Sum of the group totals of the P CTAs of the cluster, in rank order (every CTA gets the
-// same bits). One thread sends this CTA's total into every peer's shared memory with
-// st.async (completing 4 tx-bytes on the peer's mbarrier), waits (bounded) for the peers'
-// totals, and broadcasts the result to the group. Returns false, uniformly over the
-// group, when the exchange gave up.
-__device__ __forceinline__ bool cluster_sum(float& v, const StreamPlan& pl, const SmemLayout& L, int gid,
-                                            int gl, uint32_t seq, uint32_t rank, int site) {
+// Cluster exchange of a row total (rows split over the P CTAs of a cluster, one row group
+// per CTA). cluster_send (warp 0): lane 0 stores this CTA's total locally and arms the
+// slot's mbarrier for the P-1 peer totals; lane q != rank stores it into peer q's slot with
+// st.async, completing 4 tx-bytes on the peer's mbarrier. cluster_recv (every warp): waits
+// (bounded) for the slot and sums the P totals with one shuffle tree, so every warp of
+// every CTA of the cluster gets the same bits. Four slots (row number mod 4) are enough
+// with one row of lag: a peer posts row seq + 4 only after it received this CTA's row
+// seq + 2, which warp 0 sends after every warp of this CTA has read row seq (the row
+// group's named barrier in group_sum orders them).
+__device__ __forceinline__ void cluster_send(float v, const StreamPlan& pl, const SmemLayout& L, int warp,
+                                             int lane, uint32_t seq, uint32_t rank) {
+  if (warp != 0) return;
   const uint32_t slot = seq & (kXSlots - 1);
-  const uint32_t parity = (seq / kXSlots) & 1u;
   float* xp = L.xpart + slot * kMaxCluster;
-  if (gl == 0) {
+  if (lane == 0) {
     xp[rank] = v;
     mbar_arrive_expect_tx(&L.xbar[slot], static_cast<uint32_t>(pl.P - 1) * 4u);
-    const uint32_t my_slot = smem_u32(&xp[rank]);
-    const uint32_t my_bar = smem_u32(&L.xbar[slot]);
-    for (int q = 0; q < pl.P; ++q) {
-      if (q == static_cast<int>(rank)) continue;
-      st_async_peer(map_peer(my_slot, q), v, map_peer(my_bar, q));
-    }
-    const bool ok = mbar_wait<true>(&L.xbar[slot], parity, site);
-    float t = 0.f;
-    for (int q = 0; q < pl.P; ++q) t += xp[q];
-    L.bc[slot] = t;
-    L.bcf[slot] = ok ? 1 : 0;
   }
-  if (pl.G > 32) named_barrier(1 + gid, pl.G); else __syncwarp();
-  v = L.bc[slot];
-  return L.bcf[slot] != 0;
+  if (lane < pl.P && lane != static_cast<int>(rank))
+    st_async_peer(map_peer(smem_u32(&xp[rank]), lane), v, map_peer(smem_u32(&L.xbar[slot]), lane));
 }
 
-// Split form of cluster_sum for the pipelined split-row loop: cluster_send posts this
-// CTA's total for row `seq` (thread gl == 0 only, no wait); cluster_recv waits (bounded)
-// for the peers' totals of row `seq`, sums them in rank order and broadcasts the result to
-// the group. Four slots (seq mod 4) make two rows in flight safe: a peer can only post row
-// seq + 4 after it received this CTA's row seq + 2, which this CTA sends after it has read
-// row seq.
-__device__ __forceinline__ void cluster_send(float v, const StreamPlan& pl, const SmemLayout& L, int gl,
-                                             uint32_t seq, uint32_t rank) {
-  if (gl != 0) return;
+__device__ __forceinline__ float cluster_recv(const StreamPlan& pl, const SmemLayout& L, int lane, uint32_t seq,
+                                              int site) {
   const uint32_t slot = seq & (kXSlots - 1);
-  float* xp = L.xpart + slot * kMaxCluster;
-  xp[rank] = v;
-  mbar_arrive_expect_tx(&L.xbar[slot], static_cast<uint32_t>(pl.P - 1) * 4u);
-  const uint32_t my_slot = smem_u32(&xp[rank]);
-  const uint32_t my_bar = smem_u32(&L.xbar[slot]);
-  for (int q = 0; q < pl.P; ++q) {
-    if (q == static_cast<int>(rank)) continue;
-    st_async_peer(map_peer(my_slot, q), v, map_peer(my_bar, q));
-  }
-}
-
-__device__ __forceinline__ bool cluster_recv(float& v, const StreamPlan& pl, const SmemLayout& L, int gid,
-                                             int gl, uint32_t seq, int site) {
-  const uint32_t slot = seq & (kXSlots - 1);
-  if (gl == 0) {
-    const bool ok = mbar_wait<true>(&L.xbar[slot], (seq / kXSlots) & 1u, site);
-    const float* xp = L.xpart + slot * kMaxCluster;
-    float t = 0.f;
-    for (int q = 0; q < pl.P; ++q) t += xp[q];
-    L.bc[slot] = t;
-    L.bcf[slot] = ok ? 1 : 0;
-  }
-  if (pl.G > 32) named_barrier(1 + gid, pl.G); else __syncwarp();
-  v = L.bc[slot];
-  return L.bcf[slot] != 0;
+  mbar_wait<true>(&L.xbar[slot], (seq / kXSlots) & 1u, site);
+  const float* xp = L.xpart + slot * kMaxCluster;
+  return warp_sum(lane < pl.P ? xp[lane] : 0.f);
 }
 
 // xor-shuffle sum over aligned groups of `width` lanes (width a power of two <= 32).
@@ -154,11 +137,13 @@ __device__ __forceinline__ float seg_sum(float v, int width, unsigned mask) {
   return v;
 }
 
-// Waits (bounded) for the copies of tiles [consumed, issued) after a failure.
-__device__ __forceinline__ void drain_ring(const StreamPlan& pl, const SmemLayout& L, int64_t consumed,
-                                           int64_t issued) {
-  for (int64_t j = consumed; j < issued; ++j)
-    mbar_wait(&L.full[j % pl.S], static_cast<uint32_t>(j / pl.S) & 1u, kSiteDrain);
+// After a failure: let every copy still in flight land before the CTA exits (waits bounded
+// by time only). Slot s last held local tile q_last(s).
+__device__ __forceinline__ void drain_after_failure(const StreamPlan& pl, const SmemLayout& L, int64_t n_local) {
+  for (int s = 0; s < pl.S && s < n_local; ++s) {
+    const int64_t q_last = s + ((n_local - 1 - s) / pl.S) * pl.S;
+    mbar_wait(&L.full[s], static_cast<uint32_t>(q_last / pl.S) & 1u, kSiteDrain, false);
+  }
 }
 
 template <typename T>
@@ -167,10 +152,12 @@ using Elt = typename std::conditional<Present<T>::value, T, float>::type;
 // =======================================================================================
 // Forward
 // =======================================================================================
+// Local tile q (tile = cid + q * ncl) into slot s: R rows (P == 1, contiguous) or the row
+// slice of this CTA (P > 1).
 template <typename X, typename RT>
 __device__ __forceinline__ void fwd_issue(const FwdParams& p, const StreamPlan& pl, const SmemLayout& L,
-                                          unsigned char* smem, int64_t tile, int s,
-                                          int64_t slice_elt0, uint64_t pol) {
+                                          unsigned char* smem, int64_t tile, int s, int64_t slice_elt0,
+                                          uint64_t pol) {
   unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
   const int64_t row0 = tile * pl.R;
   const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
@@ -182,22 +169,6 @@ __device__ __forceinline__ void fwd_issue(const FwdParams& p, const StreamPlan& 
   bulk_load(st + pl.off[0], static_cast<const X*>(p.x) + e0, bx, &L.full[s], pol);
   if constexpr (Present<RT>::value)
     bulk_load(st + pl.off[1], static_cast<const RT*>(p.res) + e0, br, &L.full[s], pol);
-}
-
-// Split-row pipeline: sub-chunk j of the row slice of tile `tile` into ring slot `slot`.
-template <typename X, typename RT>
-__device__ __forceinline__ void fwd_issue_chunk(const FwdParams& p, const StreamPlan& pl, const SmemLayout& L,
-                                                unsigned char* smem, int64_t tile, int j, int slot,
-                                                int64_t slice_elt0, uint64_t pol) {
-  unsigned char* st = smem + static_cast<size_t>(slot) * pl.stage_bytes;
-  fence_proxy_async_smem();
-  const uint32_t bx = pl.row_bytes[0];
-  const uint32_t br = Present<RT>::value ? pl.row_bytes[1] : 0u;
-  mbar_arrive_expect_tx(&L.full[slot], bx + br);
-  const int64_t e0 = tile * pl.W + slice_elt0 + static_cast<int64_t>(j) * (pl.vslice / pl.K) * 8;
-  bulk_load(st + pl.off[0], static_cast<const X*>(p.x) + e0, bx, &L.full[slot], pol);
-  if constexpr (Present<RT>::value)
-    bulk_load(st + pl.off[1], static_cast<const RT*>(p.res) + e0, br, &L.full[slot], pol);
 }
 
 // X: input dtype; RT: residual dtype (NoT = none); OT: output dtype; ROT: residual_out
@@ -212,6 +183,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
   const StreamPlan& pl = p.pl;
   const SmemLayout L = carve_smem(smem, pl);
   const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
   uint32_t rank = 0;
   int64_t cid = blockIdx.x;
   int64_t ncl = gridDim.x;
@@ -224,21 +197,18 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
 
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const uint64_t pol = l2_policy_evict_first();
-  int64_t issued = 0;
-  if (tid == 0 && pl.P == 1) {
-    for (int j = 0; j < pl.S; ++j) {
-      const int64_t t = cid + j * ncl;
-      if (t >= pl.ntiles) break;
-      fwd_issue<X, RT>(p, pl, L, smem, t, j, slice_elt0, pol);
-      ++issued;
-    }
-  }
+  const int64_t n_local = cid < pl.ntiles ? (pl.ntiles - 1 - cid) / ncl + 1 : 0;
+  const int S = pl.S;
+  if (tid == 0)
+    for (int q = 0; q < S && q < n_local; ++q) fwd_issue<X, RT>(p, pl, L, smem, cid + q * ncl, q, slice_elt0, pol);
 
   const int G = pl.G;
   const int G8 = G * 8;
   const int gid = tid / G;
   const int gl = tid - gid * G;
   const bool in_group = gid < pl.rps;
+  const int nwarps = (pl.rps * G + 31) >> 5;  // warps with work; the others idle to the end
+  const bool active_warp = warp < nwarps;
   const float n_f = static_cast<float>(pl.N);
   unsigned vmask = 0;
 #pragma unroll
@@ -257,230 +227,146 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       if (p.b != nullptr) load8_rt(p.b, p.b_dt, p.b_per_head ? c : c % pl.N, br[k], true);
     }
   }
+  const int xs_stride = static_cast<int>(pl.row_bytes[0] / sizeof(X));  // elements per staged row
 
-  if (pl.P > 1) {
-    // ------------- split-row pipeline (row slices across a cluster, R = 1) -------------
-    // Row slices are streamed as K sub-chunks through an S-slot ring. Iteration i runs
-    // pass 1 of row i and posts its partial sum to the cluster, then (lag 1) receives
-    // row i-1's total and runs its pass 2, so the exchange overlaps a whole pass 1.
-    const int K = pl.K;
-    const int S = pl.S;
-    const int kpc_mask = (1 << pl.kpc_shift) - 1;
-    const int64_t n_local = cid < pl.ntiles ? (pl.ntiles - 1 - cid) / ncl + 1 : 0;
-    const int64_t total_q = n_local * K;
-    const bool grp = tid < G;
-    // ring positions are tracked incrementally (no 64-bit division in the loop)
-    int iss_slot = 0, iss_j = 0;
-    int64_t iss_tile = cid;
-    auto issue_upto = [&](int64_t lim) {
-      while (issued < lim) {
-        fwd_issue_chunk<X, RT>(p, pl, L, smem, iss_tile, iss_j, iss_slot, slice_elt0, pol);
-        ++issued;
-        if (++iss_slot == S) iss_slot = 0;
-        if (++iss_j == K) { iss_j = 0; iss_tile += ncl; }
-      }
-    };
-    if (tid == 0) issue_upto(min(total_q, static_cast<int64_t>(S)));
-    auto slot_ptr = [&](int base, int k, uint32_t off) -> const unsigned char* {
-      int sl = base + (k >> pl.kpc_shift);
-      if (sl >= S) sl -= S;
-      return smem + static_cast<size_t>(sl) * pl.stage_bytes + off;
-    };
-    int row_slot = 0;       // ring slot of sub-chunk 0 of row i
-    uint32_t row_phase = 0;  // its mbarrier phase parity
-    bool failed = false;
-    int64_t i = 0;
-    for (; i < n_local + pl.lag; ++i) {
-      bool ok = true;
-      if (i < n_local) {
-        for (int j = 0; j < K; ++j) {
-          int sl = row_slot + j;
-          uint32_t ph = row_phase;
-          if (sl >= S) { sl -= S; ph ^= 1u; }
-          ok = mbar_wait(&L.full[sl], ph, kSiteFwdFull) && ok;
+  // pass 2 of one staged row: writes residual_out, out and (row mode) rstd
+  auto pass2 = [&](const X* xs, const RTe* rs, int64_t row, const float (&rstd_k)[kVecs]) {
+    const int64_t g0 = row * pl.W + slice_elt0 + gl * 8;
+    OT* op = static_cast<OT*>(p.out) + g0;
+    ROe* rop = static_cast<ROe*>(p.ro) + g0;
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+      if ((vmask >> k) & 1u) {
+        float h[8];
+        Vec8<X>::load(xs + k * G8, h);
+        if constexpr (kRes) {
+          float r[8];
+          Vec8<RTe>::load(rs + k * G8, r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) h[e] += r[e];
         }
+        if constexpr (kRO) Vec8<ROe>::store(rop + k * G8, h);
+        float y[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = fmaf(h[e] * rstd_k[k], wr[k][e], br[k][e]);
+        Vec8<OT>::store(op + k * G8, y);
       }
-      if (__syncthreads_or(!ok || failed)) { failed = true; break; }
-      if (grp) {
-        const int xo = gl * 8;
-        if (i < n_local) {
+    }
+  };
+  auto pass1 = [&](const X* xs, const RTe* rs, float (&part)[kVecs]) {
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+      part[k] = 0.f;
+      if ((vmask >> k) & 1u) {
+        float h[8];
+        Vec8<X>::load(xs + k * G8, h);
+        if constexpr (kRes) {
+          float r[8];
+          Vec8<RTe>::load(rs + k * G8, r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) h[e] += r[e];
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) part[k] = fmaf(h[e], h[e], part[k]);
+      }
+    }
+  };
+  auto stage_x = [&](int s) {
+    return reinterpret_cast<const X*>(smem + static_cast<size_t>(s) * pl.stage_bytes + pl.off[0]) + gl * 8;
+  };
+  auto stage_r = [&](int s) {
+    return reinterpret_cast<const RTe*>(smem + static_cast<size_t>(s) * pl.stage_bytes + pl.off[1]) + gl * 8;
+  };
+
+  if (active_warp && pl.P == 1) {
+    // ------------------------------- tile loop -------------------------------
+    int s = 0;
+    uint32_t ph = 0;
+    uint32_t seq = 0;
+    for (int64_t q = 0; q < n_local; ++q) {
+      const int64_t tile = cid + q * ncl;
+      mbar_wait(&L.full[s], ph, kSiteFwdFull);
+      const X* xs0 = stage_x(s);
+      const RTe* rs0 = stage_r(s);
+      const int64_t row0 = tile * pl.R;
+      const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
+      for (int sw = 0; sw < pl.R; sw += pl.rps) {
+        const int lr = sw + gid;
+        const bool active = in_group && lr < rows;
+        const unsigned amask = __ballot_sync(0xffffffffu, active);
+        if (!active) continue;
+        const X* xs = xs0 + lr * xs_stride;
+        const RTe* rs = rs0 + lr * xs_stride;
+        const int64_t row = row0 + lr;
+        float part[kVecs];
+        pass1(xs, rs, part);
+        float rstd_k[kVecs];
+        if (pl.seg_mode) {
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) rstd_k[k] = rsqrtf(seg_sum(part[k], pl.vs, amask) / n_f + p.eps);
+        } else {
           float ss = 0.f;
 #pragma unroll
-          for (int k = 0; k < kVecs; ++k) {
-            if ((vmask >> k) & 1u) {
-              const int vo = xo + (k & kpc_mask) * G8;
-              float h[8];
-              Vec8<X>::load(reinterpret_cast<const X*>(slot_ptr(row_slot, k, pl.off[0])) + vo, h);
-              if constexpr (kRes) {
-                float r[8];
-                Vec8<RTe>::load(reinterpret_cast<const RTe*>(slot_ptr(row_slot, k, pl.off[1])) + vo, r);
+          for (int k = 0; k < kVecs; ++k) ss += part[k];
+          ss = group_sum(ss, pl, L, gid, gl, seq++);
+          const float r = rsqrtf(ss / n_f + p.eps);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) h[e] += r[e];
-              }
-#pragma unroll
-              for (int e = 0; e < 8; ++e) ss = fmaf(h[e], h[e], ss);
-            }
-          }
-          ss = group_sum(ss, pl, L, 0, gl, static_cast<uint32_t>(i));
-          cluster_send(ss, pl, L, gl, static_cast<uint32_t>(i), rank);
+          for (int k = 0; k < kVecs; ++k) rstd_k[k] = r;
         }
-        const int64_t r2 = i - pl.lag;
-        if (r2 >= 0 && r2 < n_local) {
-          int base2 = row_slot - pl.lag * K;
-          if (base2 < 0) base2 += S;
-          float tot;
-          if (!cluster_recv(tot, pl, L, 0, gl, static_cast<uint32_t>(r2), kSiteFwdCluster)) {
-            failed = true;
-          } else {
-            const float rs = rsqrtf(tot / n_f + p.eps);
-            const int64_t row = cid + r2 * ncl;
-            const int64_t g0 = row * pl.W + slice_elt0 + xo;
-            OT* op = static_cast<OT*>(p.out) + g0;
-            ROe* rop = static_cast<ROe*>(p.ro) + g0;
+        pass2(xs, rs, row, rstd_k);
+        if (p.rstd != nullptr) {
+          if (pl.seg_mode) {
 #pragma unroll
             for (int k = 0; k < kVecs; ++k) {
-              if ((vmask >> k) & 1u) {
-                const int vo = xo + (k & kpc_mask) * G8;
-                float h[8];
-                Vec8<X>::load(reinterpret_cast<const X*>(slot_ptr(base2, k, pl.off[0])) + vo, h);
-                if constexpr (kRes) {
-                  float r[8];
-                  Vec8<RTe>::load(reinterpret_cast<const RTe*>(slot_ptr(base2, k, pl.off[1])) + vo, r);
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) h[e] += r[e];
-                }
-                if constexpr (kRO) Vec8<ROe>::store(rop + k * G8, h);
-                float y[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) y[e] = fmaf(h[e] * rs, wr[k][e], br[k][e]);
-                Vec8<OT>::store(op + k * G8, y);
-              }
+              const int v = gl + k * G;
+              if (((vmask >> k) & 1u) && (v & (pl.vs - 1)) == 0)
+                p.rstd[row * pl.heads + (v >> pl.vs_shift)] = rstd_k[k];
             }
-            if (p.rstd != nullptr && gl == 0 && rank == 0) p.rstd[row] = rs;
+          } else if (gl == 0) {
+            p.rstd[row] = rstd_k[0];
           }
         }
       }
-      __syncthreads();  // pass 2 of row i - lag is done: its slots are free
-      if (tid == 0) issue_upto(min(total_q, max(static_cast<int64_t>(0), i + 1 - pl.lag) * K + S));
+      if (release_slot(L, s, nwarps) && q + S < n_local)
+        fwd_issue<X, RT>(p, pl, L, smem, tile + S * ncl, s, slice_elt0, pol);
+      if (++s == S) { s = 0; ph ^= 1u; }
+    }
+  } else if (active_warp) {
+    // --------- split-row loop (rows split over the cluster, one row per tile) ---------
+    // Iteration i: pass 1 of row i and its exchange, then pass 2 of row i - lag.
+    const int lag = pl.lag;
+    int s1 = 0, s2 = 0;
+    uint32_t ph1 = 0;
+    for (int64_t i = 0; i < n_local + lag; ++i) {
       if (i < n_local) {
-        row_slot += K;
-        if (row_slot >= S) { row_slot -= S; row_phase ^= 1u; }
-      }
-    }
-    failed = __syncthreads_or(failed);
-    if (failed && tid == 0) drain_ring(pl, L, i * K, issued);
-    return;
-  }
-
-  const int xs_stride = static_cast<int>(pl.row_bytes[0] / sizeof(X));  // elements per staged row
-  uint32_t seq = 0;  // rows reduced by this group (parity of scratch slots, cluster phases)
-  int64_t i = 0;
-  bool failed = false;
-  for (int64_t tile = cid; tile < pl.ntiles; tile += ncl, ++i) {
-    const int s = static_cast<int>(i % pl.S);
-    const bool ok = mbar_wait(&L.full[s], static_cast<uint32_t>(i / pl.S) & 1u, kSiteFwdFull);
-    if (__syncthreads_or(!ok || failed)) { failed = true; break; }
-    if (tid == 0 && i > 0 && pl.S > 1) {  // everyone is past tile i-1: its stage is free
-      const int64_t t = cid + (i - 1 + pl.S) * ncl;
-      if (t < pl.ntiles) {
-        fwd_issue<X, RT>(p, pl, L, smem, t, static_cast<int>((i - 1) % pl.S), slice_elt0, pol);
-        ++issued;
-      }
-    }
-    const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
-    const X* xs0 = reinterpret_cast<const X*>(st + pl.off[0]) + gl * 8;
-    const RTe* rs0 = reinterpret_cast<const RTe*>(st + pl.off[1]) + gl * 8;
-    const int64_t row0 = tile * pl.R;
-    const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
-    for (int sw = 0; sw < pl.R; sw += pl.rps) {
-      const int lr = sw + gid;
-      const bool active = in_group && lr < rows;
-      const unsigned amask = __ballot_sync(0xffffffffu, active);
-      if (!active) continue;
-      const X* xs = xs0 + lr * xs_stride;
-      const RTe* rs = rs0 + lr * xs_stride;
-      const int64_t row = row0 + lr;
-      const int64_t g0 = row * pl.W + slice_elt0 + gl * 8;
-
-      float part[kVecs];
-#pragma unroll
-      for (int k = 0; k < kVecs; ++k) {
-        part[k] = 0.f;
-        if ((vmask >> k) & 1u) {
-          float h[8];
-          Vec8<X>::load(xs + k * G8, h);
-          if constexpr (kRes) {
-            float r[8];
-            Vec8<RTe>::load(rs + k * G8, r);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) h[e] += r[e];
-          }
-#pragma unroll
-          for (int e = 0; e < 8; ++e) part[k] = fmaf(h[e], h[e], part[k]);
-        }
-      }
-
-      float rstd_k[kVecs];
-      if (pl.seg_mode) {
-#pragma unroll
-        for (int k = 0; k < kVecs; ++k) rstd_k[k] = rsqrtf(seg_sum(part[k], pl.vs, amask) / n_f + p.eps);
-      } else {
+        mbar_wait(&L.full[s1], ph1, kSiteFwdFull);
+        float part[kVecs];
+        pass1(stage_x(s1), stage_r(s1), part);
         float ss = 0.f;
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) ss += part[k];
-        ss = group_sum(ss, pl, L, gid, gl, seq);
-        if (pl.P > 1 && !cluster_sum(ss, pl, L, gid, gl, seq, rank, kSiteFwdCluster)) {
-          failed = true;
-          ++seq;
-          break;
-        }
-        ++seq;
-        const float r = rsqrtf(ss / n_f + p.eps);
-#pragma unroll
-        for (int k = 0; k < kVecs; ++k) rstd_k[k] = r;
+        ss = group_sum(ss, pl, L, 0, gl, static_cast<uint32_t>(i));
+        cluster_send(ss, pl, L, warp, lane, static_cast<uint32_t>(i), rank);
+        if (++s1 == S) { s1 = 0; ph1 ^= 1u; }
       }
-
-      OT* op = static_cast<OT*>(p.out) + g0;
-      ROe* rop = static_cast<ROe*>(p.ro) + g0;
+      const int64_t r2 = i - lag;
+      if (r2 >= 0 && r2 < n_local) {
+        const float tot = cluster_recv(pl, L, lane, static_cast<uint32_t>(r2), kSiteFwdCluster);
+        const int64_t row = cid + r2 * ncl;
+        float rstd_k[kVecs];
+        const float rs = rsqrtf(tot / n_f + p.eps);
 #pragma unroll
-      for (int k = 0; k < kVecs; ++k) {
-        if ((vmask >> k) & 1u) {
-          float h[8];
-          Vec8<X>::load(xs + k * G8, h);
-          if constexpr (kRes) {
-            float r[8];
-            Vec8<RTe>::load(rs + k * G8, r);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) h[e] += r[e];
-          }
-          if constexpr (kRO) Vec8<ROe>::store(rop + k * G8, h);
-          float y[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) y[e] = fmaf(h[e] * rstd_k[k], wr[k][e], br[k][e]);
-          Vec8<OT>::store(op + k * G8, y);
-        }
+        for (int k = 0; k < kVecs; ++k) rstd_k[k] = rs;
+        if (in_group) pass2(stage_x(s2), stage_r(s2), row, rstd_k);
+        if (p.rstd != nullptr && tid == 0 && rank == 0) p.rstd[row] = rs;
+        if (release_slot(L, s2, nwarps) && r2 + S < n_local)
+          fwd_issue<X, RT>(p, pl, L, smem, row + S * ncl, s2, slice_elt0, pol);
+        if (++s2 == S) s2 = 0;
       }
-      if (p.rstd != nullptr) {
-        if (pl.seg_mode) {
-#pragma unroll
-          for (int k = 0; k < kVecs; ++k) {
-            const int v = gl + k * G;
-            if (((vmask >> k) & 1u) && (v & (pl.vs - 1)) == 0)
-              p.rstd[row * pl.heads + (v >> pl.vs_shift)] = rstd_k[k];
-          }
-        } else if (gl == 0 && rank == 0) {
-          p.rstd[row] = rstd_k[0];
-        }
-      }
-    }
-    if (pl.S == 1) {  // a single stage is refilled once everyone is done with it
-      __syncthreads();
-      const int64_t t = cid + (i + 1) * ncl;
-      if (tid == 0 && t < pl.ntiles) { fwd_issue<X, RT>(p, pl, L, smem, t, 0, slice_elt0, pol); ++issued; }
     }
   }
-  failed = __syncthreads_or(failed);
-  if (failed && tid == 0) drain_ring(pl, L, i, issued);
+  __syncthreads();
+  if (tid == 0 && abort_requested()) drain_after_failure(pl, L, n_local);
 }
 
 // =======================================================================================
@@ -488,8 +374,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
 // =======================================================================================
 template <typename X, typename DY, typename DROT>
 __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& pl, const SmemLayout& L,
-                                          unsigned char* smem, int64_t tile, int s,
-                                          int64_t slice_elt0, int rstd_per_row, uint64_t pol) {
+                                          unsigned char* smem, int64_t tile, int s, int64_t slice_elt0,
+                                          int rstd_per_row, uint64_t pol) {
   unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
   const int64_t row0 = tile * pl.R;
   const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
@@ -514,29 +400,6 @@ __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& 
     bulk_load(st + pl.off[2], static_cast<const DROT*>(p.dro) + e0, b2, &L.full[s], pol);
 }
 
-// Split-row pipeline: sub-chunk j of the row slice of tile `tile` into ring slot `slot`;
-// sub-chunk 0 also brings the row's rstd.
-template <typename X, typename DY, typename DROT>
-__device__ __forceinline__ void bwd_issue_chunk(const BwdParams& p, const StreamPlan& pl, const SmemLayout& L,
-                                                unsigned char* smem, int64_t tile, int j, int slot,
-                                                int64_t slice_elt0, uint64_t pol) {
-  unsigned char* st = smem + static_cast<size_t>(slot) * pl.stage_bytes;
-  fence_proxy_async_smem();
-  if (j == 0) {
-    cp_async_4(st + pl.off[3], p.rstd + tile);
-    cp_async_arrive(&L.full[slot]);
-  }
-  const uint32_t b0 = pl.row_bytes[0];
-  const uint32_t b1 = pl.row_bytes[1];
-  const uint32_t b2 = Present<DROT>::value ? pl.row_bytes[2] : 0u;
-  mbar_arrive_expect_tx(&L.full[slot], b0 + b1 + b2);
-  const int64_t e0 = tile * pl.W + slice_elt0 + static_cast<int64_t>(j) * (pl.vslice / pl.K) * 8;
-  bulk_load(st + pl.off[0], static_cast<const X*>(p.x) + e0, b0, &L.full[slot], pol);
-  bulk_load(st + pl.off[1], static_cast<const DY*>(p.dy) + e0, b1, &L.full[slot], pol);
-  if constexpr (Present<DROT>::value)
-    bulk_load(st + pl.off[2], static_cast<const DROT*>(p.dro) + e0, b2, &L.full[slot], pol);
-}
-
 // X: saved input dtype; DY: dout dtype; DXT: dx dtype; DROT: dresidual_out dtype (NoT =
 // none); DREST: dresidual dtype (NoT = not written).
 template <typename X, typename DY, typename DXT, typename DROT, typename DREST, bool kHasDb, int kVecs,
@@ -550,6 +413,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   const StreamPlan& pl = p.pl;
   const SmemLayout L = carve_smem(smem, pl);
   const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
   uint32_t rank = 0;
   int64_t cid = blockIdx.x;
   int64_t ncl = gridDim.x;
@@ -563,21 +428,19 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const int rstd_per_row = pl.seg_mode ? pl.heads : 1;
   const uint64_t pol = l2_policy_evict_first();
-  int64_t issued = 0;
-  if (tid == 0 && pl.P == 1) {
-    for (int j = 0; j < pl.S; ++j) {
-      const int64_t t = cid + j * ncl;
-      if (t >= pl.ntiles) break;
-      bwd_issue<X, DY, DROT>(p, pl, L, smem, t, j, slice_elt0, rstd_per_row, pol);
-      ++issued;
-    }
-  }
+  const int64_t n_local = cid < pl.ntiles ? (pl.ntiles - 1 - cid) / ncl + 1 : 0;
+  const int S = pl.S;
+  if (tid == 0)
+    for (int q = 0; q < S && q < n_local; ++q)
+      bwd_issue<X, DY, DROT>(p, pl, L, smem, cid + q * ncl, q, slice_elt0, rstd_per_row, pol);
 
   const int G = pl.G;
   const int G8 = G * 8;
   const int gid = tid / G;
   const int gl = tid - gid * G;
   const bool in_group = gid < pl.rps;
+  const int nwarps = (pl.rps * G + 31) >> 5;
+  const bool active_warp = warp < nwarps;
   const float n_f = static_cast<float>(pl.N);
   unsigned vmask = 0;
 #pragma unroll
@@ -598,232 +461,140 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     }
     if (((vmask >> k) & 1u) && p.w != nullptr) load8_rt(p.w, p.w_dt, p.w_per_head ? c : c % pl.N, wr[k], true);
   }
+  const int x_stride = static_cast<int>(pl.row_bytes[0] / sizeof(X));
 
-  bool failed = false;
-  int64_t i = 0;
-  if (pl.P > 1) {
-    // ------------- split-row pipeline (row slices across a cluster, R = 1) -------------
-    // As in the forward: K sub-chunks per row slice through an S-slot ring; pass 1 of row
-    // i (dot product, dweight/dbias accumulation) overlaps the cluster exchange of row
-    // i-1, whose pass 2 (dx) follows.
-    const int K = pl.K;
-    const int S = pl.S;
-    const int kpc_mask = (1 << pl.kpc_shift) - 1;
-    const int64_t n_local = cid < pl.ntiles ? (pl.ntiles - 1 - cid) / ncl + 1 : 0;
-    const int64_t total_q = n_local * K;
-    const bool grp = tid < G;
-    int iss_slot = 0, iss_j = 0;
-    int64_t iss_tile = cid;
-    auto issue_upto = [&](int64_t lim) {
-      while (issued < lim) {
-        bwd_issue_chunk<X, DY, DROT>(p, pl, L, smem, iss_tile, iss_j, iss_slot, slice_elt0, pol);
-        ++issued;
-        if (++iss_slot == S) iss_slot = 0;
-        if (++iss_j == K) { iss_j = 0; iss_tile += ncl; }
-      }
-    };
-    if (tid == 0) issue_upto(min(total_q, static_cast<int64_t>(S)));
-    auto slot_base = [&](int base, int k) -> const unsigned char* {
-      int sl = base + (k >> pl.kpc_shift);
-      if (sl >= S) sl -= S;
-      return smem + static_cast<size_t>(sl) * pl.stage_bytes;
-    };
-    int row_slot = 0;
-    uint32_t row_phase = 0;
-    for (; i < n_local + pl.lag; ++i) {
-      bool ok = true;
-      if (i < n_local) {
-        for (int j = 0; j < K; ++j) {
-          int sl = row_slot + j;
-          uint32_t ph = row_phase;
-          if (sl >= S) { sl -= S; ph ^= 1u; }
-          ok = mbar_wait(&L.full[sl], ph, kSiteBwdFull) && ok;
+  struct RowPtrs {
+    const X* x;
+    const DY* dy;
+    const DROe* dro;
+    const float* rstd;  // this row's rstd block (one per segment in seg mode)
+  };
+  auto row_ptrs = [&](int s, int lr) -> RowPtrs {
+    const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
+    RowPtrs r;
+    r.x = reinterpret_cast<const X*>(st + pl.off[0]) + lr * x_stride + gl * 8;
+    r.dy = reinterpret_cast<const DY*>(st + pl.off[1]) + lr * x_stride + gl * 8;
+    r.dro = reinterpret_cast<const DROe*>(st + pl.off[2]) + lr * x_stride + gl * 8;
+    r.rstd = reinterpret_cast<const float*>(st + pl.off[3]) + lr * rstd_per_row;
+    return r;
+  };
+  // pass 1: partial dot products per vector, dweight / dbias accumulation
+  auto pass1 = [&](const RowPtrs& rp, float (&part)[kVecs], float (&rstd_k)[kVecs]) {
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+      part[k] = 0.f;
+      rstd_k[k] = 0.f;
+      if ((vmask >> k) & 1u) {
+        const float r = rp.rstd[pl.seg_mode ? ((gl + k * G) >> pl.vs_shift) : 0];
+        rstd_k[k] = r;
+        float xv[8], dv[8];
+        Vec8<X>::load(rp.x + k * G8, xv);
+        Vec8<DY>::load(rp.dy + k * G8, dv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float xh = xv[e] * r;
+          part[k] = fmaf(xh, dv[e] * wr[k][e], part[k]);
+          dw[k][e] = fmaf(dv[e], xh, dw[k][e]);
+          if constexpr (kHasDb) db[kHasDb ? k : 0][e] += dv[e];
         }
       }
-      if (__syncthreads_or(!ok || failed)) { failed = true; break; }
-      if (grp) {
-        const int xo = gl * 8;
-        if (i < n_local) {
-          const float r = *reinterpret_cast<const float*>(slot_base(row_slot, 0) + pl.off[3]);
+    }
+  };
+  // pass 2: dx (+ dresidual_out), written to dx and dresidual
+  auto pass2 = [&](const RowPtrs& rp, int64_t row, const float (&rstd_k)[kVecs], const float (&c_k)[kVecs]) {
+    const int64_t g0 = row * pl.W + slice_elt0 + gl * 8;
+    DXT* dxp = static_cast<DXT*>(p.dx) + g0;
+    DRESe* drp = static_cast<DRESe*>(p.dres) + g0;
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+      if ((vmask >> k) & 1u) {
+        const float r = rstd_k[k];
+        float xv[8], dv[8], g[8];
+        Vec8<X>::load(rp.x + k * G8, xv);
+        Vec8<DY>::load(rp.dy + k * G8, dv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) g[e] = (dv[e] * wr[k][e] - (xv[e] * r) * c_k[k]) * r;
+        if constexpr (kDro) {
+          float a[8];
+          Vec8<DROe>::load(rp.dro + k * G8, a);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) g[e] += a[e];
+        }
+        Vec8<DXT>::store(dxp + k * G8, g);
+        if constexpr (kDres) Vec8<DRESe>::store(drp + k * G8, g);
+      }
+    }
+  };
+
+  if (active_warp && pl.P == 1) {
+    // ------------------------------- tile loop -------------------------------
+    int s = 0;
+    uint32_t ph = 0;
+    uint32_t seq = 0;
+    for (int64_t q = 0; q < n_local; ++q) {
+      const int64_t tile = cid + q * ncl;
+      mbar_wait(&L.full[s], ph, kSiteBwdFull);
+      const int64_t row0 = tile * pl.R;
+      const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
+      for (int sw = 0; sw < pl.R; sw += pl.rps) {
+        const int lr = sw + gid;
+        const bool active = in_group && lr < rows;
+        const unsigned amask = __ballot_sync(0xffffffffu, active);
+        if (!active) continue;
+        const RowPtrs rp = row_ptrs(s, lr);
+        float part[kVecs], rstd_k[kVecs], c_k[kVecs];
+        pass1(rp, part, rstd_k);
+        if (pl.seg_mode) {
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) c_k[k] = seg_sum(part[k], pl.vs, amask) / n_f;
+        } else {
           float dot = 0.f;
 #pragma unroll
-          for (int k = 0; k < kVecs; ++k) {
-            if ((vmask >> k) & 1u) {
-              const int vo = xo + (k & kpc_mask) * G8;
-              const unsigned char* sb = slot_base(row_slot, k);
-              float xv[8], dv[8];
-              Vec8<X>::load(reinterpret_cast<const X*>(sb + pl.off[0]) + vo, xv);
-              Vec8<DY>::load(reinterpret_cast<const DY*>(sb + pl.off[1]) + vo, dv);
+          for (int k = 0; k < kVecs; ++k) dot += part[k];
+          const float c = group_sum(dot, pl, L, gid, gl, seq++) / n_f;
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float xh = xv[e] * r;
-                dot = fmaf(xh, dv[e] * wr[k][e], dot);
-                dw[k][e] = fmaf(dv[e], xh, dw[k][e]);
-                if constexpr (kHasDb) db[kHasDb ? k : 0][e] += dv[e];
-              }
-            }
-          }
-          dot = group_sum(dot, pl, L, 0, gl, static_cast<uint32_t>(i));
-          cluster_send(dot, pl, L, gl, static_cast<uint32_t>(i), rank);
+          for (int k = 0; k < kVecs; ++k) c_k[k] = c;
         }
-        const int64_t r2 = i - pl.lag;
-        if (r2 >= 0 && r2 < n_local) {
-          int base2 = row_slot - pl.lag * K;
-          if (base2 < 0) base2 += S;
-          float tot;
-          if (!cluster_recv(tot, pl, L, 0, gl, static_cast<uint32_t>(r2), kSiteBwdCluster)) {
-            failed = true;
-          } else {
-            const float c = tot / n_f;
-            const float r = *reinterpret_cast<const float*>(slot_base(base2, 0) + pl.off[3]);
-            const int64_t g0 = (cid + r2 * ncl) * pl.W + slice_elt0 + xo;
-            DXT* dxp = static_cast<DXT*>(p.dx) + g0;
-            DRESe* drp = static_cast<DRESe*>(p.dres) + g0;
-#pragma unroll
-            for (int k = 0; k < kVecs; ++k) {
-              if ((vmask >> k) & 1u) {
-                const int vo = xo + (k & kpc_mask) * G8;
-                const unsigned char* sb = slot_base(base2, k);
-                float xv[8], dv[8], g[8];
-                Vec8<X>::load(reinterpret_cast<const X*>(sb + pl.off[0]) + vo, xv);
-                Vec8<DY>::load(reinterpret_cast<const DY*>(sb + pl.off[1]) + vo, dv);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) g[e] = (dv[e] * wr[k][e] - (xv[e] * r) * c) * r;
-                if constexpr (kDro) {
-                  float a[8];
-                  Vec8<DROe>::load(reinterpret_cast<const DROe*>(sb + pl.off[2]) + vo, a);
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) g[e] += a[e];
-                }
-                Vec8<DXT>::store(dxp + k * G8, g);
-                if constexpr (kDres) Vec8<DRESe>::store(drp + k * G8, g);
-              }
-            }
-          }
-        }
+        pass2(rp, row0 + lr, rstd_k, c_k);
       }
-      __syncthreads();  // pass 2 of row i - lag is done: its slots are free
-      if (tid == 0) issue_upto(min(total_q, max(static_cast<int64_t>(0), i + 1 - pl.lag) * K + S));
+      if (release_slot(L, s, nwarps) && q + S < n_local)
+        bwd_issue<X, DY, DROT>(p, pl, L, smem, tile + S * ncl, s, slice_elt0, rstd_per_row, pol);
+      if (++s == S) { s = 0; ph ^= 1u; }
+    }
+  } else if (active_warp) {
+    // --------- split-row loop (rows split over the cluster, one row per tile) ---------
+    const int lag = pl.lag;
+    int s1 = 0, s2 = 0;
+    uint32_t ph1 = 0;
+    for (int64_t i = 0; i < n_local + lag; ++i) {
       if (i < n_local) {
-        row_slot += K;
-        if (row_slot >= S) { row_slot -= S; row_phase ^= 1u; }
-      }
-    }
-    failed = __syncthreads_or(failed);
-    if (failed) {
-      if (tid == 0) drain_ring(pl, L, i * K, issued);
-      return;
-    }
-  } else {
-  const int x_stride = static_cast<int>(pl.row_bytes[0] / sizeof(X));
-  uint32_t seq = 0;
-  for (int64_t tile = cid; tile < pl.ntiles; tile += ncl, ++i) {
-    const int s = static_cast<int>(i % pl.S);
-    const bool ok = mbar_wait(&L.full[s], static_cast<uint32_t>(i / pl.S) & 1u, kSiteBwdFull);
-    if (__syncthreads_or(!ok || failed)) { failed = true; break; }
-    if (tid == 0 && i > 0 && pl.S > 1) {
-      const int64_t t = cid + (i - 1 + pl.S) * ncl;
-      if (t < pl.ntiles) {
-        bwd_issue<X, DY, DROT>(p, pl, L, smem, t, static_cast<int>((i - 1) % pl.S), slice_elt0, rstd_per_row, pol);
-        ++issued;
-      }
-    }
-    const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
-    const X* xs0 = reinterpret_cast<const X*>(st + pl.off[0]) + gl * 8;
-    const DY* ds0 = reinterpret_cast<const DY*>(st + pl.off[1]) + gl * 8;
-    const DROe* as0 = reinterpret_cast<const DROe*>(st + pl.off[2]) + gl * 8;
-    const float* rs_stage = reinterpret_cast<const float*>(st + pl.off[3]);
-    const int64_t row0 = tile * pl.R;
-    const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
-    for (int sw = 0; sw < pl.R; sw += pl.rps) {
-      const int lr = sw + gid;
-      const bool active = in_group && lr < rows;
-      const unsigned amask = __ballot_sync(0xffffffffu, active);
-      if (!active) continue;
-      const X* xs = xs0 + lr * x_stride;
-      const DY* ds = ds0 + lr * x_stride;
-      const DROe* as = as0 + lr * x_stride;
-      const int64_t g0 = (row0 + lr) * pl.W + slice_elt0 + gl * 8;
-
-      float rstd_k[kVecs];
-      float part[kVecs];
-#pragma unroll
-      for (int k = 0; k < kVecs; ++k) {
-        part[k] = 0.f;
-        rstd_k[k] = 0.f;
-        if ((vmask >> k) & 1u) {
-          const float r = rs_stage[lr * rstd_per_row + (pl.seg_mode ? ((gl + k * G) >> pl.vs_shift) : 0)];
-          rstd_k[k] = r;
-          float xv[8], dv[8];
-          Vec8<X>::load(xs + k * G8, xv);
-          Vec8<DY>::load(ds + k * G8, dv);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float xh = xv[e] * r;
-            part[k] = fmaf(xh, dv[e] * wr[k][e], part[k]);
-            dw[k][e] = fmaf(dv[e], xh, dw[k][e]);
-            if constexpr (kHasDb) db[kHasDb ? k : 0][e] += dv[e];
-          }
-        }
-      }
-
-      float c_k[kVecs];
-      if (pl.seg_mode) {
-#pragma unroll
-        for (int k = 0; k < kVecs; ++k) c_k[k] = seg_sum(part[k], pl.vs, amask) / n_f;
-      } else {
+        mbar_wait(&L.full[s1], ph1, kSiteBwdFull);
+        float part[kVecs], rstd_k[kVecs];
+        pass1(row_ptrs(s1, 0), part, rstd_k);
         float dot = 0.f;
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) dot += part[k];
-        dot = group_sum(dot, pl, L, gid, gl, seq);
-        if (pl.P > 1 && !cluster_sum(dot, pl, L, gid, gl, seq, rank, kSiteBwdCluster)) {
-          failed = true;
-          ++seq;
-          break;
-        }
-        ++seq;
-        const float c = dot / n_f;
-#pragma unroll
-        for (int k = 0; k < kVecs; ++k) c_k[k] = c;
+        dot = group_sum(dot, pl, L, 0, gl, static_cast<uint32_t>(i));
+        cluster_send(dot, pl, L, warp, lane, static_cast<uint32_t>(i), rank);
+        if (++s1 == S) { s1 = 0; ph1 ^= 1u; }
       }
-
-      DXT* dxp = static_cast<DXT*>(p.dx) + g0;
-      DRESe* drp = static_cast<DRESe*>(p.dres) + g0;
+      const int64_t r2 = i - lag;
+      if (r2 >= 0 && r2 < n_local) {
+        const float c = cluster_recv(pl, L, lane, static_cast<uint32_t>(r2), kSiteBwdCluster) / n_f;
+        const int64_t row = cid + r2 * ncl;
+        const RowPtrs rp = row_ptrs(s2, 0);
+        float rstd_k[kVecs], c_k[kVecs];
 #pragma unroll
-      for (int k = 0; k < kVecs; ++k) {
-        if ((vmask >> k) & 1u) {
-          const float r = rstd_k[k];
-          float xv[8], dv[8], g[8];
-          Vec8<X>::load(xs + k * G8, xv);
-          Vec8<DY>::load(ds + k * G8, dv);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) g[e] = (dv[e] * wr[k][e] - (xv[e] * r) * c_k[k]) * r;
-          if constexpr (kDro) {
-            float a[8];
-            Vec8<DROe>::load(as + k * G8, a);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) g[e] += a[e];
-          }
-          Vec8<DXT>::store(dxp + k * G8, g);
-          if constexpr (kDres) Vec8<DRESe>::store(drp + k * G8, g);
-        }
-      }
-    }
-    if (pl.S == 1) {
-      __syncthreads();
-      const int64_t t = cid + (i + 1) * ncl;
-      if (tid == 0 && t < pl.ntiles) {
-        bwd_issue<X, DY, DROT>(p, pl, L, smem, t, 0, slice_elt0, rstd_per_row, pol);
-        ++issued;
+        for (int k = 0; k < kVecs; ++k) { rstd_k[k] = rp.rstd[0]; c_k[k] = c; }
+        if (in_group) pass2(rp, row, rstd_k, c_k);
+        if (release_slot(L, s2, nwarps) && r2 + S < n_local)
+          bwd_issue<X, DY, DROT>(p, pl, L, smem, row + S * ncl, s2, slice_elt0, rstd_per_row, pol);
+        if (++s2 == S) s2 = 0;
       }
     }
   }
-  failed = __syncthreads_or(failed);
-  if (failed) {
-    if (tid == 0) drain_ring(pl, L, i, issued);
-    return;
-  }
-  }  // tile loop
+  __syncthreads();
+  if (tid == 0 && abort_requested()) drain_after_failure(pl, L, n_local);
 
   // one partial row per (cluster, row group): the groups of a CTA own the same columns.
   // Every owned column is written, zeros included, so the reduction reads no stale data.

@@ -28,9 +28,7 @@ struct StreamPlan {
   int32_t heads;      // H
   int32_t N;          // hidden size (segment length in elements)
   int32_t nclusters;  // clusters in the grid (= CTAs when P == 1)
-  int32_t K;          // sub-chunks per row slice in the split-row pipeline (P > 1)
-  int32_t kpc_shift;  // log2(vectors per thread per sub-chunk)
-  int32_t lag;        // 1: the cluster exchange of row i overlaps pass 1 of row i+1
+  int32_t lag;        // 1: the cluster exchange of row i overlaps pass 1 of row i+1 (P > 1)
   int64_t nrows;      // super-rows
   int64_t ntiles;
   int64_t W;          // super-row width in elements (H * N)

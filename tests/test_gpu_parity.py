@@ -471,18 +471,19 @@ def test_baseline_cfg5_full(dtype):
     assert dx_err <= 1.0 and dw_err <= 1.0, (dx_err, dw_err)
 
 
-@pytest.mark.parametrize("k,lag", [(1, 0), (1, 1), (2, 0), (2, 1), (4, 0), (4, 1)])
+@pytest.mark.parametrize("lag", [0, 1])
 @pytest.mark.parametrize("dtype", [BF16, F32])
-def test_split_row_pipeline_variants(monkeypatch, k, lag, dtype):
-    """Rows split across a cluster run through the sub-chunk ring with every (K, lag)
-    combination the planner can pick; results must not depend on it."""
-    monkeypatch.setenv("RMSNORM_B200_FORCE_K", str(k))
+def test_split_row_pipeline_variants(monkeypatch, lag, dtype):
+    """Rows split across a cluster run with and without the one-row exchange lag; results
+    must not depend on it."""
     monkeypatch.setenv("RMSNORM_B200_FORCE_LAG", str(lag))
-    monkeypatch.setenv("RMSNORM_B200_FORCE_CLUSTER", "4")
+    p = 4 if dtype == BF16 else 8  # leaves room for two stages of x + residual slices
+    monkeypatch.setenv("RMSNORM_B200_FORCE_CLUSTER", str(p))
     N = 65536
     plan = _fwd_case(9, N, dtype, residual="same", bias=True, residual_dtype=F32 if dtype != F32 else None)
     if "fwd_stream" in plan:
-        assert f"K={k} lag={lag}" in plan, plan
-    plan = _bwd_case(9, N, dtype, has_bias=(k == 2))
-    if "bwd_stream" in plan and k <= (2 if k == 2 else 4):
-        assert "P=" in plan
+        assert f"lag={lag}" in plan and f"P={p}" in plan, plan
+    for has_bias in (False, True):
+        plan = _bwd_case(9, N, dtype, has_bias=has_bias)
+        if "bwd_stream" in plan:
+            assert "P=" in plan, plan
