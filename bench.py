@@ -63,6 +63,9 @@ WORKLOADS = {
                  desc="BASELINE cfg 1 shape on GPU: RMSNorm forward (8192,4096) bf16, fp32 weight"),
     "cfg3": dict(kind="bwd", rows=32768, n=65536, dtype=BF16, bias=False,
                  desc="BASELINE cfg 3: RMSNorm backward (32768,65536) bf16, fp32 weight -> dx bf16, dweight fp32"),
+    "bwd16k": dict(kind="bwd", rows=32768, n=16384, dtype=BF16, bias=False,
+                   desc="north-star target backward: RMSNorm backward (32768,16384) bf16, fp32 weight -> dx bf16, "
+                        "dweight fp32"),
     "cfg4f": dict(kind="fwd", rows=16384 * 32, n=128, heads=32, dtype=F16, residual=False, bias=True, ro=None,
                   rstd=True, desc="BASELINE cfg 4 forward: per-head (16384,32,128) fp16, (32,128) fp32 weight+bias, rstd"),
     "cfg4b": dict(kind="bwd", rows=16384 * 32, n=128, heads=32, dtype=F16, bias=True,

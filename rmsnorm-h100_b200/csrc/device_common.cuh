@@ -87,15 +87,22 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
-// One probe of phase `parity`; the hardware may suspend the thread for a short while.
+// Longest time one try_wait may keep a waiting thread suspended before it returns false.
+// The thread is woken as soon as the phase completes, so a waiting warp takes no issue
+// slots from the warps that are working; the bounded loop below re-checks its time limit
+// after every probe.
+constexpr uint32_t kSuspendHintNs = 200000;
+
+// One probe of phase `parity`; suspends the thread until the phase completes or
+// kSuspendHintNs pass.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -106,10 +113,10 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -121,17 +128,14 @@ template <bool kClusterScope>
 __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int where, bool honor_abort) {
   const uint64_t t0 = globaltimer_ns();
   const uint64_t limit = g_wait_timeout_ns;
-  uint32_t spins = 0;
   while (true) {
     if (kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) {
       return true;
     }
-    if ((++spins & 15u) == 0u) {
-      if (honor_abort && abort_requested()) return false;
-      if (globaltimer_ns() - t0 > limit) {
-        record_error(RMSNORM_B200_ERR_DEVICE_TIMEOUT, where);
-        return false;
-      }
+    if (honor_abort && abort_requested()) return false;
+    if (globaltimer_ns() - t0 > limit) {
+      record_error(RMSNORM_B200_ERR_DEVICE_TIMEOUT, where);
+      return false;
     }
   }
 }
@@ -229,6 +233,16 @@ __device__ __forceinline__ void st_async_peer(uint32_t remote_addr, float v, uin
           remote_addr),
       "r"(__float_as_uint(v)), "r"(remote_bar)
       : "memory");
+}
+
+// Global-memory accesses of the cross-CTA exchange (gpu scope; not cached in L1).
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void named_barrier(int id, int nthreads) {

@@ -56,6 +56,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 struct DeviceState {
   int sm_count = 0;
   void* noalloc_scratch = nullptr;  // device address of g_noalloc_scratch on this device
+  XRecord* xrec = nullptr;          // device address of g_xrec on this device
+  uint32_t xepoch = 0;              // launches that used the global-memory exchange
   std::mutex mu;
   std::map<const void*, bool> attrs_done;
   std::map<std::tuple<const void*, int, int, int>, int> occupancy;  // (kernel, P, smem, threads)
@@ -95,6 +97,30 @@ int noalloc_scratch(DeviceState* ds, void** out) {
     ds->noalloc_scratch = ptr;
   }
   *out = ds->noalloc_scratch;
+  return RMSNORM_B200_OK;
+}
+
+// Records of the global-memory row-total exchange (split rows on a cooperative grid): a
+// file-scope device array, kXRecSets sets used round-robin by launch epoch, so launches
+// that overlap at their ends (at most a few on one device) use different sets; a record
+// whose tag carries another epoch (31 bits) is never taken for this launch's.
+static __device__ XRecord g_xrec[kXRecSets * kXRecMaxCtas * kXSlots];
+
+// Next launch epoch (never 0, so zero-initialised records never match) and its record set.
+int next_xepoch(DeviceState* ds, XRecord** rec, uint32_t* epoch) {
+  std::lock_guard<std::mutex> lock(ds->mu);
+  if (!ds->xrec) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_xrec) != cudaSuccess || !ptr) {
+      cudaGetLastError();
+      return RMSNORM_B200_ERR_CUDA;
+    }
+    ds->xrec = static_cast<XRecord*>(ptr);
+  }
+  ds->xepoch = (ds->xepoch + 1) & 0x7fffffffu;  // the tag keeps 31 bits of the epoch
+  if (ds->xepoch == 0) ds->xepoch = 1;
+  *epoch = ds->xepoch;
+  *rec = ds->xrec + static_cast<size_t>(ds->xepoch % kXRecSets) * kXRecMaxCtas * kXSlots;
   return RMSNORM_B200_OK;
 }
 
@@ -229,14 +255,41 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
   pl.rps = P > 1 ? 1 : T / pl.G;
   if (pl.rps < 1) { *why = "group wider than the CTA"; return false; }
   pl.lag = 0;
+  pl.K = 1;
+  pl.kpc_shift = log2i(max_vecs);
 
   if (P > 1) {
-    // Split-row pipeline: one slot per row slice; lag 1 (pass 2 of row i-1 runs while
-    // row i's exchange is in flight) needs two resident rows, so S >= 2.
+    // Split-row ring: a row slice streams as K chunks (ring units). K = 1 (lag 1) when two
+    // slices fit; otherwise the slice is cut into the fewest chunks of >= 32 KB that leave
+    // at least one chunk of the next row loading behind the current row (K > 1 needs every
+    // thread to own max_vecs vectors of the slice, so a chunk holds whole thread vectors).
+    const bool full = pl.vslice == pl.G * max_vecs;
+    auto chunk_bytes = [&](int k) {
+      uint32_t off = 0;
+      for (int t = 0; t < 3; ++t) off = align_up(off + static_cast<uint32_t>(pl.vslice / k) * 8u * in_bytes[t], 128);
+      return off + (rstd_staged ? 128u : 0u);
+    };
+    const int force_k = env_int("RMSNORM_B200_FORCE_K", 0);
+    int K = 1;
+    if (force_k > 0) {
+      if (!is_pow2(force_k) || force_k > max_vecs || (force_k > 1 && !full)) {
+        *why = "forced chunk count does not divide the thread vectors";
+        return false;
+      }
+      K = force_k;
+    } else if (budget / static_cast<int>(chunk_bytes(1)) < 2 && full) {
+      for (int k = 2; k <= max_vecs; k <<= 1) {
+        if (chunk_bytes(k) < 32u * 1024u) break;
+        K = k;
+        if (budget / static_cast<int>(chunk_bytes(k)) >= k + 1) break;
+      }
+    }
+    pl.K = K;
+    pl.kpc_shift = log2i(max_vecs / K);
     pl.R = 1;
     uint32_t off = 0;
     for (int t = 0; t < 3; ++t) {
-      pl.row_bytes[t] = static_cast<uint32_t>(pl.vslice) * 8u * in_bytes[t];
+      pl.row_bytes[t] = static_cast<uint32_t>(pl.vslice / K) * 8u * in_bytes[t];
       pl.off[t] = off;
       off = align_up(off + pl.row_bytes[t], 128);
     }
@@ -245,10 +298,15 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
     pl.stage_bytes = off;
     const int max_s = std::max(1, std::min(kMaxStages, env_int("RMSNORM_B200_MAX_STAGES", kMaxStages)));
     pl.S = std::min<int>(max_s, budget / static_cast<int>(off));
-    if (pl.S < 1) { *why = "no split-row ring fits"; return false; }
+    if (pl.S < K) { *why = "no split-row ring fits"; return false; }
+    // Exchange lag: rows i-lag..i stay resident while row i's total is exchanged, which
+    // needs S >= (lag + 1) * K ring units; a deeper lag lets a CTA run ahead of its
+    // slowest peer.
     const int force_lag = env_int("RMSNORM_B200_FORCE_LAG", -1);
-    pl.lag = pl.S >= 2 ? 1 : 0;
-    if (force_lag == 0) pl.lag = 0;
+    int lag = pl.S >= 2 * K ? 1 : 0;
+    if (force_lag >= 0) lag = std::min(force_lag, rmsb200::kMaxLag);
+    while (lag > 0 && pl.S < (lag + 1) * K) --lag;
+    pl.lag = lag;
     pl.ntiles = pl.nrows;
     *out = pl;
     return true;
@@ -299,27 +357,51 @@ int smem_bytes(const StreamPlan& pl) { return pl.S * static_cast<int>(pl.stage_b
 std::string describe(const char* kind, const StreamPlan& pl, int grid) {
   char buf[512];
   std::snprintf(buf, sizeof(buf),
-                "%s mode=%s P=%d grid=%d clusters=%d T=%d G=%d rps=%d R=%d S=%d stage=%u "
-                "vslice=%d vs=%d lag=%d tiles=%lld",
-                kind, pl.seg_mode ? "seg" : "row", pl.P, grid, pl.nclusters, pl.T, pl.G, pl.rps,
-                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, pl.lag, static_cast<long long>(pl.ntiles));
+                "%s mode=%s P=%d x=%s grid=%d clusters=%d T=%d G=%d rps=%d R=%d S=%d stage=%u "
+                "vslice=%d vs=%d K=%d lag=%d tiles=%lld",
+                kind, pl.seg_mode ? "seg" : "row", pl.P,
+                pl.P == 1 ? "none" : (pl.xmode == kXGlobal ? "global" : "cluster"), grid, pl.nclusters, pl.T, pl.G,
+                pl.rps,
+                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, pl.K, pl.lag, static_cast<long long>(pl.ntiles));
   return buf;
 }
 
-// Sizes the grid (persistent: as many clusters as can be resident, at most one per tile)
-// and, unless dry_run, launches. Returns UNSUPPORTED when no cluster of this shape fits.
+// Sizes the grid (persistent: as many clusters or groups as can be resident, at most one
+// per tile), picks the row-total exchange for split rows and, unless dry_run, launches.
+// Clusters of 4, 8 or 16 CTAs fit fewer times on the GPU than the SM count allows (on
+// B200: 33 x 4, 15 x 8, 7 x 16 of 148 SMs); where groups of P CTAs of a cooperative grid
+// keep more SMs busy, those exchange through global memory instead. Returns UNSUPPORTED
+// when no cluster of this shape fits.
 template <typename Params>
 int launch_stream(DeviceState* ds, void (*kernel)(const Params), Params params, StreamPlan& pl,
                   cudaStream_t stream, const char* kind, bool dry_run, int* grid_out) {
   const int smem = smem_bytes(pl);
   if (ensure_attrs(ds, reinterpret_cast<const void*>(kernel)) != RMSNORM_B200_OK) return RMSNORM_B200_ERR_CUDA;
-  const int units = resident_units(ds, reinterpret_cast<const void*>(kernel), pl.P, smem, pl.T);
+  const void* kfn = reinterpret_cast<const void*>(kernel);
+  const int64_t ntiles = std::max<int64_t>(pl.ntiles, 1);
+  int units = resident_units(ds, kfn, pl.P, smem, pl.T);
+  pl.xmode = kXCluster;
+  if (pl.P > 1) {
+    const int ctas = std::min(resident_units(ds, kfn, 1, smem, pl.T), kXRecMaxCtas);
+    const int groups = ctas / pl.P;
+    const int force = env_int("RMSNORM_B200_XMODE", -1);  // 0 cluster, 1 global
+    const bool global = force == kXGlobal ||
+                        (force < 0 && std::min<int64_t>(ntiles, groups) > std::min<int64_t>(ntiles, units));
+    if (global && groups > 0) {
+      pl.xmode = kXGlobal;
+      units = groups;
+    }
+  }
   if (units <= 0) return RMSNORM_B200_ERR_UNSUPPORTED;
-  const int64_t nclusters = std::min<int64_t>(std::max<int64_t>(pl.ntiles, 1), units);
+  const int64_t nclusters = std::min<int64_t>(ntiles, units);
   pl.nclusters = static_cast<int>(nclusters);
   const int grid = static_cast<int>(nclusters * pl.P);
   if (grid_out) *grid_out = grid;
   if (dry_run) return RMSNORM_B200_OK;
+  params.xrec = nullptr;
+  params.xepoch = 0;
+  if (pl.xmode == kXGlobal && next_xepoch(ds, &params.xrec, &params.xepoch) != RMSNORM_B200_OK)
+    return RMSNORM_B200_ERR_CUDA;
   params.pl = pl;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -327,12 +409,19 @@ int launch_stream(DeviceState* ds, void (*kernel)(const Params), Params params, 
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = pl.P;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  if (pl.P > 1 && pl.xmode == kXCluster) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = pl.P;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.numAttrs = 1;
+  } else if (pl.P > 1) {
+    // the P CTAs of a group wait for one another: all CTAs must be resident at once
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.numAttrs = 1;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pl.P > 1 ? 1 : 0;
   const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, params);
   if (err != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
   g_launches.fetch_add(1, std::memory_order_relaxed);

@@ -34,7 +34,8 @@
 
 namespace rmsb200 {
 
-constexpr int kXSlots = 4;  // cluster exchange slots (row sequence number mod 4)
+constexpr int kXSlots = 8;  // cluster exchange slots (row sequence number mod 8)
+constexpr int kMaxLag = 3;  // deepest exchange lag the slots allow: kXSlots >= 2 * lag + 2
 
 struct SmemLayout {
   uint64_t* full;   // [kMaxStages] slot filled
@@ -65,7 +66,7 @@ __device__ __forceinline__ void init_barriers(const SmemLayout& L, const StreamP
     fence_mbar_init();
   }
   __syncthreads();
-  if (pl.P > 1) cluster_sync_all();
+  if (pl.P > 1 && pl.xmode == kXCluster) cluster_sync_all();
 }
 
 // Called by every lane of a warp after its last read of slot s. Returns true on lane 0 of
@@ -106,14 +107,46 @@ __device__ __forceinline__ float group_sum(float v, const StreamPlan& pl, const 
 // slot's mbarrier for the P-1 peer totals; lane q != rank stores it into peer q's slot with
 // st.async, completing 4 tx-bytes on the peer's mbarrier. cluster_recv (every warp): waits
 // (bounded) for the slot and sums the P totals with one shuffle tree, so every warp of
-// every CTA of the cluster gets the same bits. Four slots (row number mod 4) are enough
-// with one row of lag: a peer posts row seq + 4 only after it received this CTA's row
-// seq + 2, which warp 0 sends after every warp of this CTA has read row seq (the row
-// group's named barrier in group_sum orders them).
-__device__ __forceinline__ void cluster_send(float v, const StreamPlan& pl, const SmemLayout& L, int warp,
-                                             int lane, uint32_t seq, uint32_t rank) {
+// every CTA of the cluster gets the same bits. With an exchange lag of L rows (row r is
+// received in iteration r + L), kXSlots >= 2L + 2 slots (row number mod kXSlots) are
+// enough: a peer posts row r in iteration r, after it received this CTA's row r - L - 1,
+// which warp 0 sends in iteration r - L - 1 only after every warp of this CTA has
+// finished iteration r - L - 2 (the row group's named barrier in group_sum orders them)
+// and so has read row r - 2L - 2 <= r - kXSlots out of the slot.
+// Where the exchange goes through global memory (kXGlobal), the group's CTAs are CTAs
+// cta0 .. cta0+P-1 of one cooperative grid (all resident at once). cluster_send: lane 0 of
+// warp 0 writes the CTA's total and the row's tag as one 64-bit word into its record for
+// the slot. Every warp reads the P records itself (lane q reads rank q's): xrec_load is
+// issued a whole pass ahead (at the top of the iteration that receives the row), and
+// cluster_recv re-reads (bounded) until all P words carry the row's tag, then sums the
+// totals with the same shuffle tree as above. The slot argument above covers the records:
+// with lag <= kMaxLag a CTA rewrites its record for row r only after every warp of every
+// peer has read its row r - kXSlots, so a reader finds row r's word or row r - kXSlots's.
+struct XCtx {
+  XRecord* rec;      // this launch's record set
+  uint32_t epoch2;   // launch epoch << 1
+  int64_t cta0;      // first CTA of the group
+};
+
+__device__ __forceinline__ uint32_t xrec_tag(const XCtx& xc, uint32_t seq) {
+  return xc.epoch2 | ((seq / kXSlots) & 1u);
+}
+
+__device__ __forceinline__ XRecord xrec_load(const StreamPlan& pl, const XCtx& xc, int lane, uint32_t seq) {
+  if (pl.xmode != kXGlobal || lane >= pl.P) return 0ull;
+  return ld_relaxed_u64(xc.rec + (xc.cta0 + lane) * kXSlots + (seq & (kXSlots - 1)));
+}
+
+__device__ __forceinline__ void cluster_send(float v, const StreamPlan& pl, const SmemLayout& L, const XCtx& xc,
+                                             int warp, int lane, uint32_t seq, uint32_t rank) {
   if (warp != 0) return;
   const uint32_t slot = seq & (kXSlots - 1);
+  if (pl.xmode == kXGlobal) {
+    if (lane == 0)
+      st_relaxed_u64(xc.rec + (xc.cta0 + rank) * kXSlots + slot,
+                     (static_cast<unsigned long long>(xrec_tag(xc, seq)) << 32) | __float_as_uint(v));
+    return;
+  }
   float* xp = L.xpart + slot * kMaxCluster;
   if (lane == 0) {
     xp[rank] = v;
@@ -123,9 +156,28 @@ __device__ __forceinline__ void cluster_send(float v, const StreamPlan& pl, cons
     st_async_peer(map_peer(smem_u32(&xp[rank]), lane), v, map_peer(smem_u32(&L.xbar[slot]), lane));
 }
 
-__device__ __forceinline__ float cluster_recv(const StreamPlan& pl, const SmemLayout& L, int lane, uint32_t seq,
-                                              int site) {
+// `pre`: this lane's xrec_load for the row (kXGlobal).
+__device__ __forceinline__ float cluster_recv(const StreamPlan& pl, const SmemLayout& L, const XCtx& xc, int lane,
+                                              uint32_t seq, XRecord pre, int site) {
   const uint32_t slot = seq & (kXSlots - 1);
+  if (pl.xmode == kXGlobal) {
+    const uint32_t want = xrec_tag(xc, seq);
+    XRecord w = pre;
+    uint64_t t0 = 0;
+    while (!__all_sync(0xffffffffu, lane >= pl.P || static_cast<uint32_t>(w >> 32) == want)) {
+      if (abort_requested()) break;
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > g_wait_timeout_ns) {
+        if (lane == 0) record_error(RMSNORM_B200_ERR_DEVICE_TIMEOUT, site);
+        break;
+      }
+      __nanosleep(20);
+      w = xrec_load(pl, xc, lane, seq);
+    }
+    return warp_sum(lane < pl.P ? __uint_as_float(static_cast<uint32_t>(w)) : 0.f);
+  }
   mbar_wait<true>(&L.xbar[slot], (seq / kXSlots) & 1u, site);
   const float* xp = L.xpart + slot * kMaxCluster;
   return warp_sum(lane < pl.P ? xp[lane] : 0.f);
@@ -138,12 +190,24 @@ __device__ __forceinline__ float seg_sum(float v, int width, unsigned mask) {
 }
 
 // After a failure: let every copy still in flight land before the CTA exits (waits bounded
-// by time only). Slot s last held local tile q_last(s).
-__device__ __forceinline__ void drain_after_failure(const StreamPlan& pl, const SmemLayout& L, int64_t n_local) {
-  for (int s = 0; s < pl.S && s < n_local; ++s) {
-    const int64_t q_last = s + ((n_local - 1 - s) / pl.S) * pl.S;
-    mbar_wait(&L.full[s], static_cast<uint32_t>(q_last / pl.S) & 1u, kSiteDrain, false);
+// by time only). The ring held n_units loads (tiles, or row-slice chunks); slot s last held
+// unit u_last(s).
+__device__ __forceinline__ void drain_after_failure(const StreamPlan& pl, const SmemLayout& L, int64_t n_units) {
+  for (int s = 0; s < pl.S && s < n_units; ++s) {
+    const int64_t u_last = s + ((n_units - 1 - s) / pl.S) * pl.S;
+    mbar_wait(&L.full[s], static_cast<uint32_t>(u_last / pl.S) & 1u, kSiteDrain, false);
   }
+}
+
+// Split rows (P > 1) stream as K chunks per row slice: local row i occupies ring units
+// i*K .. i*K+K-1 (slot = unit mod S), and thread vector k lies in chunk k >> kpc_shift at
+// chunk vector (k & kpc_mask) * G + gl. Chunk j of the row whose first chunk is in slot sb
+// (phase phb) is in slot sb + j, wrapping once at most (K <= S).
+__device__ __forceinline__ int chunk_slot(int sb, uint32_t phb, int j, int S, uint32_t* ph) {
+  int s = sb + j;
+  *ph = phb;
+  if (s >= S) { s -= S; *ph ^= 1u; }
+  return s;
 }
 
 template <typename T>
@@ -152,11 +216,11 @@ using Elt = typename std::conditional<Present<T>::value, T, float>::type;
 // =======================================================================================
 // Forward
 // =======================================================================================
-// Local tile q (tile = cid + q * ncl) into slot s: R rows (P == 1, contiguous) or the row
-// slice of this CTA (P > 1).
+// Tile `tile` into slot s: R rows (P == 1, contiguous), or chunk j of the row slice of this
+// CTA (P > 1; a chunk holds row_bytes[0] / sizeof(X) elements of the slice).
 template <typename X, typename RT>
 __device__ __forceinline__ void fwd_issue(const FwdParams& p, const StreamPlan& pl, const SmemLayout& L,
-                                          unsigned char* smem, int64_t tile, int s, int64_t slice_elt0,
+                                          unsigned char* smem, int64_t tile, int j, int s, int64_t slice_elt0,
                                           uint64_t pol) {
   unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
   const int64_t row0 = tile * pl.R;
@@ -165,7 +229,8 @@ __device__ __forceinline__ void fwd_issue(const FwdParams& p, const StreamPlan& 
   const uint32_t bx = static_cast<uint32_t>(rows) * pl.row_bytes[0];
   const uint32_t br = Present<RT>::value ? static_cast<uint32_t>(rows) * pl.row_bytes[1] : 0u;
   mbar_arrive_expect_tx(&L.full[s], bx + br);
-  const int64_t e0 = row0 * pl.W + slice_elt0;  // P > 1 implies R == 1
+  // P > 1 implies R == 1
+  const int64_t e0 = row0 * pl.W + slice_elt0 + static_cast<int64_t>(j) * (pl.row_bytes[0] / sizeof(X));
   bulk_load(st + pl.off[0], static_cast<const X*>(p.x) + e0, bx, &L.full[s], pol);
   if constexpr (Present<RT>::value)
     bulk_load(st + pl.off[1], static_cast<const RT*>(p.res) + e0, br, &L.full[s], pol);
@@ -189,18 +254,29 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
   int64_t cid = blockIdx.x;
   int64_t ncl = gridDim.x;
   if (pl.P > 1) {
-    rank = cluster_ctarank();
-    cid = cluster_id_x();
-    ncl = cluster_count_x();
+    if (pl.xmode == kXCluster) {
+      rank = cluster_ctarank();
+      cid = cluster_id_x();
+      ncl = cluster_count_x();
+    } else {
+      rank = blockIdx.x % pl.P;
+      cid = blockIdx.x / pl.P;
+      ncl = gridDim.x / pl.P;
+    }
   }
+  const XCtx xc{p.xrec, p.xepoch << 1, cid * pl.P};
   init_barriers(L, pl);
 
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const uint64_t pol = l2_policy_evict_first();
   const int64_t n_local = cid < pl.ntiles ? (pl.ntiles - 1 - cid) / ncl + 1 : 0;
   const int S = pl.S;
+  const int K = pl.K;
+  const int kshift = __ffs(K) - 1;
+  const int64_t n_units = n_local * K;
   if (tid == 0)
-    for (int q = 0; q < S && q < n_local; ++q) fwd_issue<X, RT>(p, pl, L, smem, cid + q * ncl, q, slice_elt0, pol);
+    for (int u = 0; u < S && u < n_units; ++u)
+      fwd_issue<X, RT>(p, pl, L, smem, cid + (u >> kshift) * ncl, u & (K - 1), u, slice_elt0, pol);
 
   const int G = pl.G;
   const int G8 = G * 8;
@@ -277,6 +353,59 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
   auto stage_r = [&](int s) {
     return reinterpret_cast<const RTe*>(smem + static_cast<size_t>(s) * pl.stage_bytes + pl.off[1]) + gl * 8;
   };
+  // the same two passes over a split row held as K > 1 chunks, first chunk in slot sb
+  const int kpc_shift = pl.kpc_shift;
+  const int kpc_mask = (1 << kpc_shift) - 1;
+  auto chunk_off = [&](int sb, int k) {  // byte offset of thread vector k's slot
+    int s = sb + (k >> kpc_shift);
+    if (s >= S) s -= S;
+    return static_cast<size_t>(s) * pl.stage_bytes;
+  };
+  auto pass1c = [&](int sb, float (&part)[kVecs]) {
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+      part[k] = 0.f;
+      if ((vmask >> k) & 1u) {
+        const size_t so = chunk_off(sb, k);
+        const int o = (k & kpc_mask) * G8 + gl * 8;
+        float h[8];
+        Vec8<X>::load(reinterpret_cast<const X*>(smem + so + pl.off[0]) + o, h);
+        if constexpr (kRes) {
+          float r[8];
+          Vec8<RTe>::load(reinterpret_cast<const RTe*>(smem + so + pl.off[1]) + o, r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) h[e] += r[e];
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) part[k] = fmaf(h[e], h[e], part[k]);
+      }
+    }
+  };
+  auto pass2c = [&](int sb, int64_t row, float rstd) {
+    const int64_t g0 = row * pl.W + slice_elt0 + gl * 8;
+    OT* op = static_cast<OT*>(p.out) + g0;
+    ROe* rop = static_cast<ROe*>(p.ro) + g0;
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+      if ((vmask >> k) & 1u) {
+        const size_t so = chunk_off(sb, k);
+        const int o = (k & kpc_mask) * G8 + gl * 8;
+        float h[8];
+        Vec8<X>::load(reinterpret_cast<const X*>(smem + so + pl.off[0]) + o, h);
+        if constexpr (kRes) {
+          float r[8];
+          Vec8<RTe>::load(reinterpret_cast<const RTe*>(smem + so + pl.off[1]) + o, r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) h[e] += r[e];
+        }
+        if constexpr (kRO) Vec8<ROe>::store(rop + k * G8, h);
+        float y[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = fmaf(h[e] * rstd, wr[k][e], br[k][e]);
+        Vec8<OT>::store(op + k * G8, y);
+      }
+    }
+  };
 
   if (active_warp && pl.P == 1) {
     // ------------------------------- tile loop -------------------------------
@@ -328,7 +457,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
         }
       }
       if (release_slot(L, s, nwarps) && q + S < n_local)
-        fwd_issue<X, RT>(p, pl, L, smem, tile + S * ncl, s, slice_elt0, pol);
+        fwd_issue<X, RT>(p, pl, L, smem, tile + S * ncl, 0, s, slice_elt0, pol);
       if (++s == S) { s = 0; ph ^= 1u; }
     }
   } else if (active_warp) {
@@ -338,43 +467,75 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
     int s1 = 0, s2 = 0;
     uint32_t ph1 = 0;
     for (int64_t i = 0; i < n_local + lag; ++i) {
+      const int64_t r2 = i - lag;
+      const XRecord pre = r2 >= 0 ? xrec_load(pl, xc, lane, static_cast<uint32_t>(r2)) : 0ull;
       if (i < n_local) {
-        mbar_wait(&L.full[s1], ph1, kSiteFwdFull);
         float part[kVecs];
-        pass1(stage_x(s1), stage_r(s1), part);
+        if (K == 1) {
+          mbar_wait(&L.full[s1], ph1, kSiteFwdFull);
+          pass1(stage_x(s1), stage_r(s1), part);
+        } else {
+          for (int j = 0; j < K; ++j) {
+            uint32_t ph;
+            const int s = chunk_slot(s1, ph1, j, S, &ph);
+            mbar_wait(&L.full[s], ph, kSiteFwdFull);
+          }
+          pass1c(s1, part);
+        }
         float ss = 0.f;
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) ss += part[k];
         ss = group_sum(ss, pl, L, 0, gl, static_cast<uint32_t>(i));
-        cluster_send(ss, pl, L, warp, lane, static_cast<uint32_t>(i), rank);
-        if (++s1 == S) { s1 = 0; ph1 ^= 1u; }
+        cluster_send(ss, pl, L, xc, warp, lane, static_cast<uint32_t>(i), rank);
+        s1 += K;
+        if (s1 >= S) { s1 -= S; ph1 ^= 1u; }
       }
-      const int64_t r2 = i - lag;
       if (r2 >= 0 && r2 < n_local) {
-        const float tot = cluster_recv(pl, L, lane, static_cast<uint32_t>(r2), kSiteFwdCluster);
+        const float tot = cluster_recv(pl, L, xc, lane, static_cast<uint32_t>(r2), pre, kSiteFwdCluster);
         const int64_t row = cid + r2 * ncl;
         float rstd_k[kVecs];
         const float rs = rsqrtf(tot / n_f + p.eps);
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) rstd_k[k] = rs;
-        if (in_group) pass2(stage_x(s2), stage_r(s2), row, rstd_k);
+        if (in_group) {
+          if (K == 1) pass2(stage_x(s2), stage_r(s2), row, rstd_k);
+          else pass2c(s2, row, rs);
+        }
         if (p.rstd != nullptr && tid == 0 && rank == 0) p.rstd[row] = rs;
-        if (release_slot(L, s2, nwarps) && r2 + S < n_local)
-          fwd_issue<X, RT>(p, pl, L, smem, row + S * ncl, s2, slice_elt0, pol);
-        if (++s2 == S) s2 = 0;
+        if (K == 1) {
+          if (release_slot(L, s2, nwarps) && r2 + S < n_local)
+            fwd_issue<X, RT>(p, pl, L, smem, row + S * ncl, 0, s2, slice_elt0, pol);
+          if (++s2 == S) s2 = 0;
+        } else {
+          for (int j = 0; j < K; ++j) {
+            uint32_t ph;
+            const int s = chunk_slot(s2, 0u, j, S, &ph);
+            const int64_t un = r2 * K + j + S;  // unit that refills the slot
+            if (release_slot(L, s, nwarps) && un < n_units)
+              fwd_issue<X, RT>(p, pl, L, smem, cid + (un >> kshift) * ncl, static_cast<int>(un & (K - 1)), s,
+                               slice_elt0, pol);
+          }
+          s2 += K;
+          if (s2 >= S) s2 -= S;
+        }
       }
     }
   }
   __syncthreads();
-  if (tid == 0 && abort_requested()) drain_after_failure(pl, L, n_local);
+  if (tid == 0 && abort_requested()) drain_after_failure(pl, L, n_units);
+  // no CTA leaves while a peer may still store into its shared memory (after a failure a
+  // peer can be rows behind)
+  if (pl.P > 1 && pl.xmode == kXCluster) cluster_sync_all();
 }
 
 // =======================================================================================
 // Backward: dx in one pass from the saved rstd; dweight / dbias per-CTA partial rows.
 // =======================================================================================
+// Tile `tile` (or chunk j of this CTA's slice of row `tile`) into slot s; every chunk of a
+// split row carries the row's rstd.
 template <typename X, typename DY, typename DROT>
 __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& pl, const SmemLayout& L,
-                                          unsigned char* smem, int64_t tile, int s, int64_t slice_elt0,
+                                          unsigned char* smem, int64_t tile, int j, int s, int64_t slice_elt0,
                                           int rstd_per_row, uint64_t pol) {
   unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
   const int64_t row0 = tile * pl.R;
@@ -384,16 +545,16 @@ __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& 
   float* rdst = reinterpret_cast<float*>(st + pl.off[3]);
   const float* rsrc = p.rstd + row0 * rstd_per_row;
   const int cnt = rows * rstd_per_row;
-  int j = 0;
+  int c = 0;
   if ((reinterpret_cast<uintptr_t>(rsrc) & 15u) == 0)
-    for (; j + 4 <= cnt; j += 4) cp_async_16(rdst + j, rsrc + j);
-  for (; j < cnt; ++j) cp_async_4(rdst + j, rsrc + j);
+    for (; c + 4 <= cnt; c += 4) cp_async_16(rdst + c, rsrc + c);
+  for (; c < cnt; ++c) cp_async_4(rdst + c, rsrc + c);
   cp_async_arrive(&L.full[s]);
   const uint32_t b0 = static_cast<uint32_t>(rows) * pl.row_bytes[0];
   const uint32_t b1 = static_cast<uint32_t>(rows) * pl.row_bytes[1];
   const uint32_t b2 = Present<DROT>::value ? static_cast<uint32_t>(rows) * pl.row_bytes[2] : 0u;
   mbar_arrive_expect_tx(&L.full[s], b0 + b1 + b2);
-  const int64_t e0 = row0 * pl.W + slice_elt0;
+  const int64_t e0 = row0 * pl.W + slice_elt0 + static_cast<int64_t>(j) * (pl.row_bytes[0] / sizeof(X));
   bulk_load(st + pl.off[0], static_cast<const X*>(p.x) + e0, b0, &L.full[s], pol);
   bulk_load(st + pl.off[1], static_cast<const DY*>(p.dy) + e0, b1, &L.full[s], pol);
   if constexpr (Present<DROT>::value)
@@ -419,10 +580,17 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   int64_t cid = blockIdx.x;
   int64_t ncl = gridDim.x;
   if (pl.P > 1) {
-    rank = cluster_ctarank();
-    cid = cluster_id_x();
-    ncl = cluster_count_x();
+    if (pl.xmode == kXCluster) {
+      rank = cluster_ctarank();
+      cid = cluster_id_x();
+      ncl = cluster_count_x();
+    } else {
+      rank = blockIdx.x % pl.P;
+      cid = blockIdx.x / pl.P;
+      ncl = gridDim.x / pl.P;
+    }
   }
+  const XCtx xc{p.xrec, p.xepoch << 1, cid * pl.P};
   init_barriers(L, pl);
 
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
@@ -430,9 +598,13 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   const uint64_t pol = l2_policy_evict_first();
   const int64_t n_local = cid < pl.ntiles ? (pl.ntiles - 1 - cid) / ncl + 1 : 0;
   const int S = pl.S;
+  const int K = pl.K;
+  const int kshift = __ffs(K) - 1;
+  const int64_t n_units = n_local * K;
   if (tid == 0)
-    for (int q = 0; q < S && q < n_local; ++q)
-      bwd_issue<X, DY, DROT>(p, pl, L, smem, cid + q * ncl, q, slice_elt0, rstd_per_row, pol);
+    for (int u = 0; u < S && u < n_units; ++u)
+      bwd_issue<X, DY, DROT>(p, pl, L, smem, cid + (u >> kshift) * ncl, u & (K - 1), u, slice_elt0, rstd_per_row,
+                             pol);
 
   const int G = pl.G;
   const int G8 = G * 8;
@@ -525,6 +697,65 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
       }
     }
   };
+  // the same two passes over a split row held as K > 1 chunks, first chunk in slot sb
+  // (every chunk carries the row's rstd; the first chunk's copy is used)
+  const int kpc_shift = pl.kpc_shift;
+  const int kpc_mask = (1 << kpc_shift) - 1;
+  auto chunk_ptrs = [&](int sb, int k) -> RowPtrs {
+    int s = sb + (k >> kpc_shift);
+    if (s >= S) s -= S;
+    const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
+    const int o = (k & kpc_mask) * G8 + gl * 8;
+    RowPtrs r;
+    r.x = reinterpret_cast<const X*>(st + pl.off[0]) + o;
+    r.dy = reinterpret_cast<const DY*>(st + pl.off[1]) + o;
+    r.dro = reinterpret_cast<const DROe*>(st + pl.off[2]) + o;
+    r.rstd = nullptr;
+    return r;
+  };
+  auto pass1c = [&](int sb, float r, float (&part)[kVecs]) {
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+      part[k] = 0.f;
+      if ((vmask >> k) & 1u) {
+        const RowPtrs cp = chunk_ptrs(sb, k);
+        float xv[8], dv[8];
+        Vec8<X>::load(cp.x, xv);
+        Vec8<DY>::load(cp.dy, dv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float xh = xv[e] * r;
+          part[k] = fmaf(xh, dv[e] * wr[k][e], part[k]);
+          dw[k][e] = fmaf(dv[e], xh, dw[k][e]);
+          if constexpr (kHasDb) db[kHasDb ? k : 0][e] += dv[e];
+        }
+      }
+    }
+  };
+  auto pass2c = [&](int sb, int64_t row, float r, float c) {
+    const int64_t g0 = row * pl.W + slice_elt0 + gl * 8;
+    DXT* dxp = static_cast<DXT*>(p.dx) + g0;
+    DRESe* drp = static_cast<DRESe*>(p.dres) + g0;
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+      if ((vmask >> k) & 1u) {
+        const RowPtrs cp = chunk_ptrs(sb, k);
+        float xv[8], dv[8], g[8];
+        Vec8<X>::load(cp.x, xv);
+        Vec8<DY>::load(cp.dy, dv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) g[e] = (dv[e] * wr[k][e] - (xv[e] * r) * c) * r;
+        if constexpr (kDro) {
+          float a[8];
+          Vec8<DROe>::load(cp.dro, a);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) g[e] += a[e];
+        }
+        Vec8<DXT>::store(dxp + k * G8, g);
+        if constexpr (kDres) Vec8<DRESe>::store(drp + k * G8, g);
+      }
+    }
+  };
 
   if (active_warp && pl.P == 1) {
     // ------------------------------- tile loop -------------------------------
@@ -558,7 +789,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
         pass2(rp, row0 + lr, rstd_k, c_k);
       }
       if (release_slot(L, s, nwarps) && q + S < n_local)
-        bwd_issue<X, DY, DROT>(p, pl, L, smem, tile + S * ncl, s, slice_elt0, rstd_per_row, pol);
+        bwd_issue<X, DY, DROT>(p, pl, L, smem, tile + S * ncl, 0, s, slice_elt0, rstd_per_row, pol);
       if (++s == S) { s = 0; ph ^= 1u; }
     }
   } else if (active_warp) {
@@ -567,34 +798,60 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     int s1 = 0, s2 = 0;
     uint32_t ph1 = 0;
     for (int64_t i = 0; i < n_local + lag; ++i) {
+      const int64_t r2 = i - lag;
+      const XRecord pre = r2 >= 0 ? xrec_load(pl, xc, lane, static_cast<uint32_t>(r2)) : 0ull;
       if (i < n_local) {
-        mbar_wait(&L.full[s1], ph1, kSiteBwdFull);
-        float part[kVecs], rstd_k[kVecs];
-        pass1(row_ptrs(s1, 0), part, rstd_k);
+        float part[kVecs];
+        if (K == 1) {
+          mbar_wait(&L.full[s1], ph1, kSiteBwdFull);
+          float rstd_k[kVecs];
+          pass1(row_ptrs(s1, 0), part, rstd_k);
+        } else {
+          for (int j = 0; j < K; ++j) {
+            uint32_t ph;
+            const int s = chunk_slot(s1, ph1, j, S, &ph);
+            mbar_wait(&L.full[s], ph, kSiteBwdFull);
+          }
+          pass1c(s1, row_ptrs(s1, 0).rstd[0], part);
+        }
         float dot = 0.f;
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) dot += part[k];
         dot = group_sum(dot, pl, L, 0, gl, static_cast<uint32_t>(i));
-        cluster_send(dot, pl, L, warp, lane, static_cast<uint32_t>(i), rank);
-        if (++s1 == S) { s1 = 0; ph1 ^= 1u; }
+        cluster_send(dot, pl, L, xc, warp, lane, static_cast<uint32_t>(i), rank);
+        s1 += K;
+        if (s1 >= S) { s1 -= S; ph1 ^= 1u; }
       }
-      const int64_t r2 = i - lag;
       if (r2 >= 0 && r2 < n_local) {
-        const float c = cluster_recv(pl, L, lane, static_cast<uint32_t>(r2), kSiteBwdCluster) / n_f;
+        const float c = cluster_recv(pl, L, xc, lane, static_cast<uint32_t>(r2), pre, kSiteBwdCluster) / n_f;
         const int64_t row = cid + r2 * ncl;
         const RowPtrs rp = row_ptrs(s2, 0);
-        float rstd_k[kVecs], c_k[kVecs];
+        if (in_group) {
+          if (K == 1) {
+            float rstd_k[kVecs], c_k[kVecs];
 #pragma unroll
-        for (int k = 0; k < kVecs; ++k) { rstd_k[k] = rp.rstd[0]; c_k[k] = c; }
-        if (in_group) pass2(rp, row, rstd_k, c_k);
-        if (release_slot(L, s2, nwarps) && r2 + S < n_local)
-          bwd_issue<X, DY, DROT>(p, pl, L, smem, row + S * ncl, s2, slice_elt0, rstd_per_row, pol);
-        if (++s2 == S) s2 = 0;
+            for (int k = 0; k < kVecs; ++k) { rstd_k[k] = rp.rstd[0]; c_k[k] = c; }
+            pass2(rp, row, rstd_k, c_k);
+          } else {
+            pass2c(s2, row, rp.rstd[0], c);
+          }
+        }
+        for (int j = 0; j < K; ++j) {
+          uint32_t ph;
+          const int s = chunk_slot(s2, 0u, j, S, &ph);
+          const int64_t un = r2 * K + j + S;  // unit that refills the slot
+          if (release_slot(L, s, nwarps) && un < n_units)
+            bwd_issue<X, DY, DROT>(p, pl, L, smem, cid + (un >> kshift) * ncl, static_cast<int>(un & (K - 1)), s,
+                                   slice_elt0, rstd_per_row, pol);
+        }
+        s2 += K;
+        if (s2 >= S) s2 -= S;
       }
     }
   }
   __syncthreads();
-  if (tid == 0 && abort_requested()) drain_after_failure(pl, L, n_local);
+  if (tid == 0 && abort_requested()) drain_after_failure(pl, L, n_units);
+  if (pl.P > 1 && pl.xmode == kXCluster) cluster_sync_all();
 
   // one partial row per (cluster, row group): the groups of a CTA own the same columns.
   // Every owned column is written, zeros included, so the reduction reads no stale data.

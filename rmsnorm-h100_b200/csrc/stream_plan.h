@@ -11,7 +11,10 @@ namespace rmsb200 {
 //   segment   : one normalisation row (N elements) inside a super-row.
 //   vector    : 8 consecutive elements (16 B for fp16/bf16, 32 B for fp32).
 //   slice     : the part of a super-row one CTA owns. Equal to the super-row unless the
-//               row is split across a thread-block cluster of P CTAs (P > 1).
+//               row is split across a group of P CTAs (P > 1): a thread-block cluster whose
+//               CTAs exchange row totals through distributed shared memory, or -- where
+//               clusters of P CTAs would leave SMs idle -- P CTAs of one cooperative grid
+//               that exchange them through tagged records in global memory.
 //   tile      : R consecutive super-rows staged into one shared-memory stage by TMA.
 //   sweep     : rps super-rows processed concurrently by rps thread groups of G threads.
 struct StreamPlan {
@@ -28,7 +31,11 @@ struct StreamPlan {
   int32_t heads;      // H
   int32_t N;          // hidden size (segment length in elements)
   int32_t nclusters;  // clusters in the grid (= CTAs when P == 1)
-  int32_t lag;        // 1: the cluster exchange of row i overlaps pass 1 of row i+1 (P > 1)
+  int32_t K;          // ring units (chunks) per row slice: 1, or 2 / 4 for split rows (P > 1)
+  int32_t kpc_shift;  // log2(thread vectors per chunk) = log2(kVecs / K)
+  int32_t xmode;      // P > 1: kXCluster (DSMEM exchange) or kXGlobal (global-memory records)
+  int32_t lag;        // rows the cluster exchange lags pass 1 by (P > 1): pass 2 of row i-lag
+                      // follows pass 1 of row i
   int64_t nrows;      // super-rows
   int64_t ntiles;
   int64_t W;          // super-row width in elements (H * N)
@@ -44,7 +51,20 @@ constexpr int kBlockLarge = 512;
 constexpr int kBlockSmall = 256;
 constexpr int kMaxStages = 16;
 constexpr int kMaxCluster = 16;
-constexpr int kSmemReserve = 1024;   // barriers + reduction scratch after the stages
+constexpr int kSmemReserve = 1280;   // barriers + reduction scratch after the stages
+
+// Row-total exchange of split rows (StreamPlan::xmode).
+constexpr int kXCluster = 0;
+constexpr int kXGlobal = 1;
+
+// One row total of one CTA in the global-memory exchange, in one 64-bit word written and
+// read whole (single-copy atomic): high half = tag, low half = the float's bits. Tag =
+// (launch epoch << 1) | (bit 0 of row / kXSlots): a reader waiting for a row finds either
+// that row's word or the one of the row kXSlots before it in the same record, or a word
+// of an earlier launch (another epoch).
+using XRecord = unsigned long long;
+constexpr int kXRecSets = 4;        // record sets, used round-robin by launch epoch
+constexpr int kXRecMaxCtas = 512;   // CTAs of a global-exchange grid
 
 struct FwdParams {
   StreamPlan pl;
@@ -58,6 +78,8 @@ struct FwdParams {
   int32_t w_dt, b_dt;
   int32_t w_per_head, b_per_head;  // 1 when the affine tensor is [H, N]
   float eps;
+  XRecord* xrec;   // kXGlobal: this launch's record set ([kXRecMaxCtas][kXSlots])
+  uint32_t xepoch; // kXGlobal: launch epoch (never 0 modulo 2^31)
 };
 
 struct BwdParams {
@@ -73,6 +95,8 @@ struct BwdParams {
   float* db_part;   // [nclusters][W] fp32 or null
   int32_t w_dt;
   int32_t w_per_head;
+  XRecord* xrec;   // as in FwdParams
+  uint32_t xepoch;
 };
 
 }  // namespace rmsb200

@@ -122,14 +122,17 @@ class LibraryError(RuntimeError):
 
 
 def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
-    """Loads librmsnorm_b200.so once and declares every exported signature."""
+    """Loads librmsnorm_b200.so once and declares every exported signature. The library
+    is the in-tree build unless `path` or the RMSNORM_B200_LIBRARY environment variable
+    names another build of the same ABI."""
     global _LIB
     if _LIB is not None and path is None:
         return _LIB
     with _LOCK:
         if _LIB is not None and path is None:
             return _LIB
-        lib_path = Path(path) if path is not None else LIB_PATH
+        env_path = os.environ.get("RMSNORM_B200_LIBRARY")
+        lib_path = Path(path) if path is not None else (Path(env_path) if env_path else LIB_PATH)
         if not lib_path.exists():
             raise LibraryError(
                 f"rmsnorm-b200 native library not found at {lib_path}; build it with "

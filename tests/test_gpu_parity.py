@@ -471,19 +471,45 @@ def test_baseline_cfg5_full(dtype):
     assert dx_err <= 1.0 and dw_err <= 1.0, (dx_err, dw_err)
 
 
-@pytest.mark.parametrize("lag", [0, 1])
+@pytest.mark.parametrize("p", [2, 4, 16])
 @pytest.mark.parametrize("dtype", [BF16, F32])
-def test_split_row_pipeline_variants(monkeypatch, lag, dtype):
-    """Rows split across a cluster run with and without the one-row exchange lag; results
-    must not depend on it."""
+def test_split_row_global_exchange(monkeypatch, p, dtype):
+    """Split rows whose totals go through tagged records in global memory (groups of P CTAs
+    of a cooperative grid) give the same results as the cluster exchange; row counts below,
+    at and above the group count of the grid, with and without the exchange lag."""
+    monkeypatch.setenv("RMSNORM_B200_XMODE", "1")
+    monkeypatch.setenv("RMSNORM_B200_FORCE_CLUSTER", str(p))
+    N = 8192 * p if dtype == BF16 else 4096 * p
+    for rows, lag in ((3, 1), (70, 1), (301, 0), (301, 1)):
+        monkeypatch.setenv("RMSNORM_B200_FORCE_LAG", str(lag))
+        plan = _fwd_case(rows, N, dtype, residual="same", bias=True, seed=rows)
+        if "fwd_stream" in plan:
+            assert f"P={p} x=global" in plan, plan
+        plan = _bwd_case(rows, N, dtype, has_bias=(rows == 70), seed=rows + 7)
+        if "bwd_stream" in plan and f"P={p}" in plan:
+            assert "x=global" in plan, plan
+    assert _lib.device_status(DEV) == (0, 0)
+
+
+@pytest.mark.parametrize("k,lag", [(1, 0), (1, 1), (1, 2), (1, 3), (2, 0), (2, 1), (2, 3), (4, 0), (4, 1)])
+@pytest.mark.parametrize("dtype", [BF16, F32])
+def test_split_row_pipeline_variants(monkeypatch, k, lag, dtype):
+    """Rows split across a cluster stream as K chunks per row slice, with an exchange lag of
+    0 to 3 rows; results must not depend on either."""
+    import re
+    monkeypatch.setenv("RMSNORM_B200_FORCE_K", str(k))
     monkeypatch.setenv("RMSNORM_B200_FORCE_LAG", str(lag))
     p = 4 if dtype == BF16 else 8  # leaves room for two stages of x + residual slices
     monkeypatch.setenv("RMSNORM_B200_FORCE_CLUSTER", str(p))
     N = 65536
     plan = _fwd_case(9, N, dtype, residual="same", bias=True, residual_dtype=F32 if dtype != F32 else None)
     if "fwd_stream" in plan:
-        assert f"lag={lag}" in plan and f"P={p}" in plan, plan
+        stages = int(re.search(r" S=(\d+)", plan).group(1))
+        want_lag = lag
+        while want_lag > 0 and stages < (want_lag + 1) * k:
+            want_lag -= 1
+        assert f"P={p}" in plan and f"K={k} lag={want_lag}" in plan, plan
     for has_bias in (False, True):
         plan = _bwd_case(9, N, dtype, has_bias=has_bias)
         if "bwd_stream" in plan:
-            assert "P=" in plan, plan
+            assert "P=" in plan and f"K={k}" in plan, plan
