@@ -477,6 +477,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="time eager launches instead of a graph replay")
     ap.add_argument("--rows", type=int, default=0, help="override the rows per rank (profiling runs)")
+    ap.add_argument("--hidden", type=int, default=0, help="override the hidden size (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -484,6 +485,9 @@ def main():
     if args.rows:
         w["rows"] = args.rows - args.rows % w.get("heads", 1)
         w["desc"] += f" [rows overridden: {w['rows']}]"
+    if args.hidden:
+        w["n"] = args.hidden
+        w["desc"] += f" [hidden overridden: {w['n']}]"
 
     if args.impl == "reference":
         run_reference_arm(args, w)

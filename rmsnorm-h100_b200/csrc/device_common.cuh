@@ -87,22 +87,15 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
-// Longest time one try_wait may keep a waiting thread suspended before it returns false.
-// The thread is woken as soon as the phase completes, so a waiting warp takes no issue
-// slots from the warps that are working; the bounded loop below re-checks its time limit
-// after every probe.
-constexpr uint32_t kSuspendHintNs = 200000;
-
-// One probe of phase `parity`; suspends the thread until the phase completes or
-// kSuspendHintNs pass.
+// One probe of phase `parity`; the hardware may suspend the thread for a short while.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
@@ -113,10 +106,10 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
@@ -170,6 +163,13 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
       "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(smem_dst)),
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
+}
+
+// Bulk prefetch of global memory into L2 (no shared-memory destination, no completion):
+// warms the lines a later bulk_load of the same range will read. Source 16-byte aligned,
+// size a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
 }
 
 // Non-bulk async copy of 4 or 16 bytes; completion is attached to an mbarrier with
@@ -349,6 +349,95 @@ struct Vec8<__half> {
   }
 };
 
+// The same 8-element vectors held as 4 float pairs, for the paired fp32 instructions of
+// sm_100 (__ffma2_rn / __fmul2_rn / __fadd2_rn: two lanes per instruction, each rounded
+// exactly as the scalar instruction). Pair i holds elements 2i and 2i+1.
+template <typename T>
+struct Pair8;
+
+template <>
+struct Pair8<float> {
+  __device__ __forceinline__ static void load(const void* p, float2 (&v)[4]) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0];
+    const float4 b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = make_float2(a.x, a.y); v[1] = make_float2(a.z, a.w);
+    v[2] = make_float2(b.x, b.y); v[3] = make_float2(b.z, b.w);
+  }
+  __device__ __forceinline__ static void load_global(const void* p, float2 (&v)[4]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = make_float2(a.x, a.y); v[1] = make_float2(a.z, a.w);
+    v[2] = make_float2(b.x, b.y); v[3] = make_float2(b.z, b.w);
+  }
+  __device__ __forceinline__ static void store(void* p, const float2 (&v)[4]) {
+    __stcs(reinterpret_cast<float4*>(p), make_float4(v[0].x, v[0].y, v[1].x, v[1].y));
+    __stcs(reinterpret_cast<float4*>(p) + 1, make_float4(v[2].x, v[2].y, v[3].x, v[3].y));
+  }
+};
+
+__device__ __forceinline__ float2 unpack_bf16x2_pair(uint32_t u) {
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2_pair(float2 v) {
+  __nv_bfloat162 h = __float22bfloat162_rn(v);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float2 unpack_f16x2_pair(uint32_t u) {
+  return __half22float2(*reinterpret_cast<__half2*>(&u));
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2_pair(float2 v) {
+  __half2 h = __float22half2_rn(v);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <>
+struct Pair8<__nv_bfloat16> {
+  __device__ __forceinline__ static void unpack(const uint4 u, float2 (&v)[4]) {
+    v[0] = unpack_bf16x2_pair(u.x); v[1] = unpack_bf16x2_pair(u.y);
+    v[2] = unpack_bf16x2_pair(u.z); v[3] = unpack_bf16x2_pair(u.w);
+  }
+  __device__ __forceinline__ static void load(const void* p, float2 (&v)[4]) {
+    unpack(*reinterpret_cast<const uint4*>(p), v);
+  }
+  __device__ __forceinline__ static void load_global(const void* p, float2 (&v)[4]) {
+    unpack(__ldg(reinterpret_cast<const uint4*>(p)), v);
+  }
+  __device__ __forceinline__ static void store(void* p, const float2 (&v)[4]) {
+    uint4 u;
+    u.x = pack_bf16x2_pair(v[0]); u.y = pack_bf16x2_pair(v[1]);
+    u.z = pack_bf16x2_pair(v[2]); u.w = pack_bf16x2_pair(v[3]);
+    __stcs(reinterpret_cast<uint4*>(p), u);
+  }
+};
+
+template <>
+struct Pair8<__half> {
+  __device__ __forceinline__ static void unpack(const uint4 u, float2 (&v)[4]) {
+    v[0] = unpack_f16x2_pair(u.x); v[1] = unpack_f16x2_pair(u.y);
+    v[2] = unpack_f16x2_pair(u.z); v[3] = unpack_f16x2_pair(u.w);
+  }
+  __device__ __forceinline__ static void load(const void* p, float2 (&v)[4]) {
+    unpack(*reinterpret_cast<const uint4*>(p), v);
+  }
+  __device__ __forceinline__ static void load_global(const void* p, float2 (&v)[4]) {
+    unpack(__ldg(reinterpret_cast<const uint4*>(p)), v);
+  }
+  __device__ __forceinline__ static void store(void* p, const float2 (&v)[4]) {
+    uint4 u;
+    u.x = pack_f16x2_pair(v[0]); u.y = pack_f16x2_pair(v[1]);
+    u.z = pack_f16x2_pair(v[2]); u.w = pack_f16x2_pair(v[3]);
+    __stcs(reinterpret_cast<uint4*>(p), u);
+  }
+};
+
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 splat2(float a) { return make_float2(a, a); }
+
 // Tag type for a tensor that is absent from a kernel instantiation.
 struct NoT {};
 template <typename T>
@@ -375,6 +464,18 @@ __device__ __forceinline__ void load8_rt(const void* base, int dt, int64_t e, fl
   } else {
     const __half* p = reinterpret_cast<const __half*>(base) + e;
     if (global) Vec8<__half>::load_global(p, v); else Vec8<__half>::load(p, v);
+  }
+}
+
+// Paired form of load8_rt (affine parameters of the streaming kernels, read from global
+// memory once per kernel).
+__device__ __forceinline__ void load8p_rt(const void* base, int dt, int64_t e, float2 (&v)[4]) {
+  if (dt == RMSNORM_B200_F32) {
+    Pair8<float>::load_global(reinterpret_cast<const float*>(base) + e, v);
+  } else if (dt == RMSNORM_B200_BF16) {
+    Pair8<__nv_bfloat16>::load_global(reinterpret_cast<const __nv_bfloat16*>(base) + e, v);
+  } else {
+    Pair8<__half>::load_global(reinterpret_cast<const __half*>(base) + e, v);
   }
 }
 

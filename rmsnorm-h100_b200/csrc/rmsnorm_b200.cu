@@ -188,6 +188,16 @@ bool is_pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
 
 uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
+// L2 prefetch distance: each refill of a ring slot can also prefetch the unit S further
+// on, so a unit's bytes are requested about 2S units before they are consumed while only S
+// units of shared memory hold them. Measured on B200 it pays only where a row slice fills
+// shared memory and streams as chunks (K > 1); elsewhere the extra L2 traffic costs more
+// than the deeper pipeline gains.
+void set_prefetch(StreamPlan& pl) {
+  const int force = env_int("RMSNORM_B200_L2_PREFETCH", -1);  // units; 0 = off
+  pl.pf = force >= 0 ? force : (pl.K > 1 ? pl.S : 0);
+}
+
 // Builds the thread/tile/stage/cluster plan for a streaming kernel launched with block
 // shape `bc`. `in_bytes[k]` is the element size of staged input k (0 = absent);
 // `rstd_staged` adds the per-row rstd block (backward); `max_vecs` is the kernel's vectors
@@ -308,6 +318,7 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
     while (lag > 0 && pl.S < (lag + 1) * K) --lag;
     pl.lag = lag;
     pl.ntiles = pl.nrows;
+    set_prefetch(pl);
     *out = pl;
     return true;
   }
@@ -348,21 +359,23 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
   const int max_s = std::max(1, std::min(kMaxStages, env_int("RMSNORM_B200_MAX_STAGES", kMaxStages)));
   pl.S = std::max(1, std::min<int>(max_s, budget / static_cast<int>(stage)));
   pl.ntiles = (pl.nrows + R - 1) / R;
+  set_prefetch(pl);
   *out = pl;
   return true;
 }
 
 int smem_bytes(const StreamPlan& pl) { return pl.S * static_cast<int>(pl.stage_bytes) + kSmemReserve; }
 
+
 std::string describe(const char* kind, const StreamPlan& pl, int grid) {
   char buf[512];
   std::snprintf(buf, sizeof(buf),
                 "%s mode=%s P=%d x=%s grid=%d clusters=%d T=%d G=%d rps=%d R=%d S=%d stage=%u "
-                "vslice=%d vs=%d K=%d lag=%d tiles=%lld",
+                "vslice=%d vs=%d K=%d lag=%d pf=%d tiles=%lld",
                 kind, pl.seg_mode ? "seg" : "row", pl.P,
                 pl.P == 1 ? "none" : (pl.xmode == kXGlobal ? "global" : "cluster"), grid, pl.nclusters, pl.T, pl.G,
                 pl.rps,
-                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, pl.K, pl.lag, static_cast<long long>(pl.ntiles));
+                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, pl.K, pl.lag, pl.pf, static_cast<long long>(pl.ntiles));
   return buf;
 }
 

@@ -218,10 +218,11 @@ using Elt = typename std::conditional<Present<T>::value, T, float>::type;
 // =======================================================================================
 // Tile `tile` into slot s: R rows (P == 1, contiguous), or chunk j of the row slice of this
 // CTA (P > 1; a chunk holds row_bytes[0] / sizeof(X) elements of the slice).
+// With pf_tile >= 0, also prefetches tile pf_tile (chunk pf_j) into L2.
 template <typename X, typename RT>
 __device__ __forceinline__ void fwd_issue(const FwdParams& p, const StreamPlan& pl, const SmemLayout& L,
                                           unsigned char* smem, int64_t tile, int j, int s, int64_t slice_elt0,
-                                          uint64_t pol) {
+                                          uint64_t pol, int64_t pf_tile = -1, int pf_j = 0) {
   unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
   const int64_t row0 = tile * pl.R;
   const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
@@ -234,6 +235,14 @@ __device__ __forceinline__ void fwd_issue(const FwdParams& p, const StreamPlan& 
   bulk_load(st + pl.off[0], static_cast<const X*>(p.x) + e0, bx, &L.full[s], pol);
   if constexpr (Present<RT>::value)
     bulk_load(st + pl.off[1], static_cast<const RT*>(p.res) + e0, br, &L.full[s], pol);
+  if (pf_tile >= 0) {
+    const int64_t prow0 = pf_tile * pl.R;
+    const uint32_t prows = static_cast<uint32_t>(min(static_cast<int64_t>(pl.R), pl.nrows - prow0));
+    const int64_t pe0 = prow0 * pl.W + slice_elt0 + static_cast<int64_t>(pf_j) * (pl.row_bytes[0] / sizeof(X));
+    bulk_prefetch_l2(static_cast<const X*>(p.x) + pe0, prows * pl.row_bytes[0]);
+    if constexpr (Present<RT>::value)
+      bulk_prefetch_l2(static_cast<const RT*>(p.res) + pe0, prows * pl.row_bytes[1]);
+  }
 }
 
 // X: input dtype; RT: residual dtype (NoT = none); OT: output dtype; ROT: residual_out
@@ -274,9 +283,15 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
   const int K = pl.K;
   const int kshift = __ffs(K) - 1;
   const int64_t n_units = n_local * K;
+  // loads unit u into slot s and prefetches unit u + pf into L2
+  auto issue_unit = [&](int64_t u, int s) {
+    const int64_t v = u + pl.pf;
+    const bool pf = pl.pf > 0 && v < n_units;
+    fwd_issue<X, RT>(p, pl, L, smem, cid + (u >> kshift) * ncl, static_cast<int>(u & (K - 1)), s, slice_elt0, pol,
+                     pf ? cid + (v >> kshift) * ncl : -1, static_cast<int>(v & (K - 1)));
+  };
   if (tid == 0)
-    for (int u = 0; u < S && u < n_units; ++u)
-      fwd_issue<X, RT>(p, pl, L, smem, cid + (u >> kshift) * ncl, u & (K - 1), u, slice_elt0, pol);
+    for (int u = 0; u < S && u < n_units; ++u) issue_unit(u, u);
 
   const int G = pl.G;
   const int G8 = G * 8;
@@ -291,19 +306,72 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
   for (int k = 0; k < kVecs; ++k)
     if (in_group && gl + k * G < pl.vslice) vmask |= 1u << k;
 
-  float wr[kVecs][8];
-  float br[kVecs][8];
+  // weight / bias of the thread's columns, as float pairs (element 2i in .x, 2i+1 in .y)
+  float2 wr[kVecs][4];
+  float2 br[kVecs][4];
 #pragma unroll
   for (int k = 0; k < kVecs; ++k) {
     const int64_t c = slice_elt0 + static_cast<int64_t>(gl + k * G) * 8;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) { wr[k][e] = 1.f; br[k][e] = 0.f; }
+    for (int i = 0; i < 4; ++i) { wr[k][i] = splat2(1.f); br[k][i] = splat2(0.f); }
     if ((vmask >> k) & 1u) {
-      if (p.w != nullptr) load8_rt(p.w, p.w_dt, p.w_per_head ? c : c % pl.N, wr[k], true);
-      if (p.b != nullptr) load8_rt(p.b, p.b_dt, p.b_per_head ? c : c % pl.N, br[k], true);
+      if (p.w != nullptr) load8p_rt(p.w, p.w_dt, p.w_per_head ? c : c % pl.N, wr[k]);
+      if (p.b != nullptr) load8p_rt(p.b, p.b_dt, p.b_per_head ? c : c % pl.N, br[k]);
     }
   }
   const int xs_stride = static_cast<int>(pl.row_bytes[0] / sizeof(X));  // elements per staged row
+
+  // Per-vector arithmetic. Without a residual the paired fp32 instructions are used; with
+  // one (x + residual, residual_out stored) the scalar form measured faster on B200. Both
+  // round every operation the same way; only the order of the sum of squares differs.
+  constexpr bool kPaired = !kRes;
+  // pass 1 of one vector: sum of squares of the pre-norm values h = x (+ residual)
+  auto sumsq = [&](const X* xp, const RTe* rp) {
+    if constexpr (kPaired) {
+      float2 h[4];
+      Pair8<X>::load(xp, h);
+      float2 acc = mul2(h[0], h[0]);
+#pragma unroll
+      for (int i = 1; i < 4; ++i) acc = fma2(h[i], h[i], acc);
+      return acc.x + acc.y;
+    } else {
+      float h[8], r[8];
+      Vec8<X>::load(xp, h);
+      Vec8<RTe>::load(rp, r);
+      float acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        h[e] += r[e];
+        acc = fmaf(h[e], h[e], acc);
+      }
+      return acc;
+    }
+  };
+  // pass 2 of thread vector k: residual_out = h, out = h * rstd * w + b
+  auto emit = [&](const X* xp, const RTe* rp, OT* op, ROe* rop, float rstd, int k) {
+    if constexpr (kPaired) {
+      float2 h[4], y[4];
+      Pair8<X>::load(xp, h);
+      if constexpr (kRO) Pair8<ROe>::store(rop, h);
+      const float2 r2 = splat2(rstd);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[i] = fma2(mul2(h[i], r2), wr[k][i], br[k][i]);
+      Pair8<OT>::store(op, y);
+    } else {
+      float h[8], r[8], y[8];
+      Vec8<X>::load(xp, h);
+      Vec8<RTe>::load(rp, r);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[e] += r[e];
+      if constexpr (kRO) Vec8<ROe>::store(rop, h);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float2 w2 = wr[k][e >> 1], b2 = br[k][e >> 1];
+        y[e] = fmaf(h[e] * rstd, (e & 1) ? w2.y : w2.x, (e & 1) ? b2.y : b2.x);
+      }
+      Vec8<OT>::store(op, y);
+    }
+  };
 
   // pass 2 of one staged row: writes residual_out, out and (row mode) rstd
   auto pass2 = [&](const X* xs, const RTe* rs, int64_t row, const float (&rstd_k)[kVecs]) {
@@ -311,41 +379,12 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
     OT* op = static_cast<OT*>(p.out) + g0;
     ROe* rop = static_cast<ROe*>(p.ro) + g0;
 #pragma unroll
-    for (int k = 0; k < kVecs; ++k) {
-      if ((vmask >> k) & 1u) {
-        float h[8];
-        Vec8<X>::load(xs + k * G8, h);
-        if constexpr (kRes) {
-          float r[8];
-          Vec8<RTe>::load(rs + k * G8, r);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) h[e] += r[e];
-        }
-        if constexpr (kRO) Vec8<ROe>::store(rop + k * G8, h);
-        float y[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) y[e] = fmaf(h[e] * rstd_k[k], wr[k][e], br[k][e]);
-        Vec8<OT>::store(op + k * G8, y);
-      }
-    }
+    for (int k = 0; k < kVecs; ++k)
+      if ((vmask >> k) & 1u) emit(xs + k * G8, rs + k * G8, op + k * G8, rop + k * G8, rstd_k[k], k);
   };
   auto pass1 = [&](const X* xs, const RTe* rs, float (&part)[kVecs]) {
 #pragma unroll
-    for (int k = 0; k < kVecs; ++k) {
-      part[k] = 0.f;
-      if ((vmask >> k) & 1u) {
-        float h[8];
-        Vec8<X>::load(xs + k * G8, h);
-        if constexpr (kRes) {
-          float r[8];
-          Vec8<RTe>::load(rs + k * G8, r);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) h[e] += r[e];
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) part[k] = fmaf(h[e], h[e], part[k]);
-      }
-    }
+    for (int k = 0; k < kVecs; ++k) part[k] = ((vmask >> k) & 1u) ? sumsq(xs + k * G8, rs + k * G8) : 0.f;
   };
   auto stage_x = [&](int s) {
     return reinterpret_cast<const X*>(smem + static_cast<size_t>(s) * pl.stage_bytes + pl.off[0]) + gl * 8;
@@ -368,16 +407,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       if ((vmask >> k) & 1u) {
         const size_t so = chunk_off(sb, k);
         const int o = (k & kpc_mask) * G8 + gl * 8;
-        float h[8];
-        Vec8<X>::load(reinterpret_cast<const X*>(smem + so + pl.off[0]) + o, h);
-        if constexpr (kRes) {
-          float r[8];
-          Vec8<RTe>::load(reinterpret_cast<const RTe*>(smem + so + pl.off[1]) + o, r);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) h[e] += r[e];
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) part[k] = fmaf(h[e], h[e], part[k]);
+        part[k] = sumsq(reinterpret_cast<const X*>(smem + so + pl.off[0]) + o,
+                        reinterpret_cast<const RTe*>(smem + so + pl.off[1]) + o);
       }
     }
   };
@@ -390,19 +421,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       if ((vmask >> k) & 1u) {
         const size_t so = chunk_off(sb, k);
         const int o = (k & kpc_mask) * G8 + gl * 8;
-        float h[8];
-        Vec8<X>::load(reinterpret_cast<const X*>(smem + so + pl.off[0]) + o, h);
-        if constexpr (kRes) {
-          float r[8];
-          Vec8<RTe>::load(reinterpret_cast<const RTe*>(smem + so + pl.off[1]) + o, r);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) h[e] += r[e];
-        }
-        if constexpr (kRO) Vec8<ROe>::store(rop + k * G8, h);
-        float y[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) y[e] = fmaf(h[e] * rstd, wr[k][e], br[k][e]);
-        Vec8<OT>::store(op + k * G8, y);
+        emit(reinterpret_cast<const X*>(smem + so + pl.off[0]) + o,
+             reinterpret_cast<const RTe*>(smem + so + pl.off[1]) + o, op + k * G8, rop + k * G8, rstd, k);
       }
     }
   };
@@ -457,7 +477,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
         }
       }
       if (release_slot(L, s, nwarps) && q + S < n_local)
-        fwd_issue<X, RT>(p, pl, L, smem, tile + S * ncl, 0, s, slice_elt0, pol);
+        issue_unit(q + S, s);
       if (++s == S) { s = 0; ph ^= 1u; }
     }
   } else if (active_warp) {
@@ -504,7 +524,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
         if (p.rstd != nullptr && tid == 0 && rank == 0) p.rstd[row] = rs;
         if (K == 1) {
           if (release_slot(L, s2, nwarps) && r2 + S < n_local)
-            fwd_issue<X, RT>(p, pl, L, smem, row + S * ncl, 0, s2, slice_elt0, pol);
+            issue_unit(r2 + S, s2);
           if (++s2 == S) s2 = 0;
         } else {
           for (int j = 0; j < K; ++j) {
@@ -512,8 +532,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
             const int s = chunk_slot(s2, 0u, j, S, &ph);
             const int64_t un = r2 * K + j + S;  // unit that refills the slot
             if (release_slot(L, s, nwarps) && un < n_units)
-              fwd_issue<X, RT>(p, pl, L, smem, cid + (un >> kshift) * ncl, static_cast<int>(un & (K - 1)), s,
-                               slice_elt0, pol);
+              issue_unit(un, s);
           }
           s2 += K;
           if (s2 >= S) s2 -= S;
@@ -536,7 +555,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
 template <typename X, typename DY, typename DROT>
 __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& pl, const SmemLayout& L,
                                           unsigned char* smem, int64_t tile, int j, int s, int64_t slice_elt0,
-                                          int rstd_per_row, uint64_t pol) {
+                                          int rstd_per_row, uint64_t pol, int64_t pf_tile = -1, int pf_j = 0) {
   unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
   const int64_t row0 = tile * pl.R;
   const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
@@ -559,6 +578,15 @@ __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& 
   bulk_load(st + pl.off[1], static_cast<const DY*>(p.dy) + e0, b1, &L.full[s], pol);
   if constexpr (Present<DROT>::value)
     bulk_load(st + pl.off[2], static_cast<const DROT*>(p.dro) + e0, b2, &L.full[s], pol);
+  if (pf_tile >= 0) {
+    const int64_t prow0 = pf_tile * pl.R;
+    const uint32_t prows = static_cast<uint32_t>(min(static_cast<int64_t>(pl.R), pl.nrows - prow0));
+    const int64_t pe0 = prow0 * pl.W + slice_elt0 + static_cast<int64_t>(pf_j) * (pl.row_bytes[0] / sizeof(X));
+    bulk_prefetch_l2(static_cast<const X*>(p.x) + pe0, prows * pl.row_bytes[0]);
+    bulk_prefetch_l2(static_cast<const DY*>(p.dy) + pe0, prows * pl.row_bytes[1]);
+    if constexpr (Present<DROT>::value)
+      bulk_prefetch_l2(static_cast<const DROT*>(p.dro) + pe0, prows * pl.row_bytes[2]);
+  }
 }
 
 // X: saved input dtype; DY: dout dtype; DXT: dx dtype; DROT: dresidual_out dtype (NoT =
@@ -601,10 +629,15 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   const int K = pl.K;
   const int kshift = __ffs(K) - 1;
   const int64_t n_units = n_local * K;
+  // loads unit u into slot s and prefetches unit u + pf into L2
+  auto issue_unit = [&](int64_t u, int s) {
+    const int64_t v = u + pl.pf;
+    const bool pf = pl.pf > 0 && v < n_units;
+    bwd_issue<X, DY, DROT>(p, pl, L, smem, cid + (u >> kshift) * ncl, static_cast<int>(u & (K - 1)), s, slice_elt0,
+                           rstd_per_row, pol, pf ? cid + (v >> kshift) * ncl : -1, static_cast<int>(v & (K - 1)));
+  };
   if (tid == 0)
-    for (int u = 0; u < S && u < n_units; ++u)
-      bwd_issue<X, DY, DROT>(p, pl, L, smem, cid + (u >> kshift) * ncl, u & (K - 1), u, slice_elt0, rstd_per_row,
-                             pol);
+    for (int u = 0; u < S && u < n_units; ++u) issue_unit(u, u);
 
   const int G = pl.G;
   const int G8 = G * 8;
@@ -619,21 +652,59 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   for (int k = 0; k < kVecs; ++k)
     if (in_group && gl + k * G < pl.vslice) vmask |= 1u << k;
 
-  float wr[kVecs][8];
-  float dw[kVecs][8];
-  float db[kHasDb ? kVecs : 1][8];
+  // weight of the thread's columns and its dweight / dbias accumulators, as float pairs
+  float2 wr[kVecs][4];
+  float2 dw[kVecs][4];
+  float2 db[kHasDb ? kVecs : 1][4];
 #pragma unroll
   for (int k = 0; k < kVecs; ++k) {
     const int64_t c = slice_elt0 + static_cast<int64_t>(gl + k * G) * 8;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) { wr[k][e] = 1.f; dw[k][e] = 0.f; }
+    for (int i = 0; i < 4; ++i) { wr[k][i] = splat2(1.f); dw[k][i] = splat2(0.f); }
     if constexpr (kHasDb) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) db[kHasDb ? k : 0][e] = 0.f;
+      for (int i = 0; i < 4; ++i) db[kHasDb ? k : 0][i] = splat2(0.f);
     }
-    if (((vmask >> k) & 1u) && p.w != nullptr) load8_rt(p.w, p.w_dt, p.w_per_head ? c : c % pl.N, wr[k], true);
+    if (((vmask >> k) & 1u) && p.w != nullptr) load8p_rt(p.w, p.w_dt, p.w_per_head ? c : c % pl.N, wr[k]);
   }
   const int x_stride = static_cast<int>(pl.row_bytes[0] / sizeof(X));
+
+  // pass 1 of thread vector k with row rstd r: returns r * sum(x * dy * w) over the
+  // vector and adds dy * x * r to dweight (dy to dbias)
+  auto dot_acc = [&](const X* xp, const DY* dp, float r, int k) {
+    float2 xv[4], dv[4];
+    Pair8<X>::load(xp, xv);
+    Pair8<DY>::load(dp, dv);
+    const float2 r2 = splat2(r);
+    float2 acc = splat2(0.f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = mul2(xv[i], dv[i]);
+      acc = fma2(t, wr[k][i], acc);
+      dw[k][i] = fma2(t, r2, dw[k][i]);
+      if constexpr (kHasDb) db[kHasDb ? k : 0][i] = add2(db[kHasDb ? k : 0][i], dv[i]);
+    }
+    return (acc.x + acc.y) * r;
+  };
+  // pass 2 of thread vector k: dx = r * dy * w - r^2 c x (+ dresidual_out), stored to dx
+  // and dresidual
+  auto dx_emit = [&](const X* xp, const DY* dp, const DROe* ap, DXT* dxo, DRESe* dro, float r, float c, int k) {
+    float2 xv[4], dv[4], g[4];
+    Pair8<X>::load(xp, xv);
+    Pair8<DY>::load(dp, dv);
+    const float2 rr = splat2(r);
+    const float2 nb = splat2(-(r * r) * c);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) g[i] = fma2(mul2(dv[i], wr[k][i]), rr, mul2(xv[i], nb));
+    if constexpr (kDro) {
+      float2 a[4];
+      Pair8<DROe>::load(ap, a);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) g[i] = add2(g[i], a[i]);
+    }
+    Pair8<DXT>::store(dxo, g);
+    if constexpr (kDres) Pair8<DRESe>::store(dro, g);
+  };
 
   struct RowPtrs {
     const X* x;
@@ -659,16 +730,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
       if ((vmask >> k) & 1u) {
         const float r = rp.rstd[pl.seg_mode ? ((gl + k * G) >> pl.vs_shift) : 0];
         rstd_k[k] = r;
-        float xv[8], dv[8];
-        Vec8<X>::load(rp.x + k * G8, xv);
-        Vec8<DY>::load(rp.dy + k * G8, dv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float xh = xv[e] * r;
-          part[k] = fmaf(xh, dv[e] * wr[k][e], part[k]);
-          dw[k][e] = fmaf(dv[e], xh, dw[k][e]);
-          if constexpr (kHasDb) db[kHasDb ? k : 0][e] += dv[e];
-        }
+        part[k] = dot_acc(rp.x + k * G8, rp.dy + k * G8, r, k);
       }
     }
   };
@@ -678,24 +740,9 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     DXT* dxp = static_cast<DXT*>(p.dx) + g0;
     DRESe* drp = static_cast<DRESe*>(p.dres) + g0;
 #pragma unroll
-    for (int k = 0; k < kVecs; ++k) {
-      if ((vmask >> k) & 1u) {
-        const float r = rstd_k[k];
-        float xv[8], dv[8], g[8];
-        Vec8<X>::load(rp.x + k * G8, xv);
-        Vec8<DY>::load(rp.dy + k * G8, dv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) g[e] = (dv[e] * wr[k][e] - (xv[e] * r) * c_k[k]) * r;
-        if constexpr (kDro) {
-          float a[8];
-          Vec8<DROe>::load(rp.dro + k * G8, a);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) g[e] += a[e];
-        }
-        Vec8<DXT>::store(dxp + k * G8, g);
-        if constexpr (kDres) Vec8<DRESe>::store(drp + k * G8, g);
-      }
-    }
+    for (int k = 0; k < kVecs; ++k)
+      if ((vmask >> k) & 1u)
+        dx_emit(rp.x + k * G8, rp.dy + k * G8, rp.dro + k * G8, dxp + k * G8, drp + k * G8, rstd_k[k], c_k[k], k);
   };
   // the same two passes over a split row held as K > 1 chunks, first chunk in slot sb
   // (every chunk carries the row's rstd; the first chunk's copy is used)
@@ -719,16 +766,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
       part[k] = 0.f;
       if ((vmask >> k) & 1u) {
         const RowPtrs cp = chunk_ptrs(sb, k);
-        float xv[8], dv[8];
-        Vec8<X>::load(cp.x, xv);
-        Vec8<DY>::load(cp.dy, dv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float xh = xv[e] * r;
-          part[k] = fmaf(xh, dv[e] * wr[k][e], part[k]);
-          dw[k][e] = fmaf(dv[e], xh, dw[k][e]);
-          if constexpr (kHasDb) db[kHasDb ? k : 0][e] += dv[e];
-        }
+        part[k] = dot_acc(cp.x, cp.dy, r, k);
       }
     }
   };
@@ -740,19 +778,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     for (int k = 0; k < kVecs; ++k) {
       if ((vmask >> k) & 1u) {
         const RowPtrs cp = chunk_ptrs(sb, k);
-        float xv[8], dv[8], g[8];
-        Vec8<X>::load(cp.x, xv);
-        Vec8<DY>::load(cp.dy, dv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) g[e] = (dv[e] * wr[k][e] - (xv[e] * r) * c) * r;
-        if constexpr (kDro) {
-          float a[8];
-          Vec8<DROe>::load(cp.dro, a);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) g[e] += a[e];
-        }
-        Vec8<DXT>::store(dxp + k * G8, g);
-        if constexpr (kDres) Vec8<DRESe>::store(drp + k * G8, g);
+        dx_emit(cp.x, cp.dy, cp.dro, dxp + k * G8, drp + k * G8, r, c, k);
       }
     }
   };
@@ -789,7 +815,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
         pass2(rp, row0 + lr, rstd_k, c_k);
       }
       if (release_slot(L, s, nwarps) && q + S < n_local)
-        bwd_issue<X, DY, DROT>(p, pl, L, smem, tile + S * ncl, 0, s, slice_elt0, rstd_per_row, pol);
+        issue_unit(q + S, s);
       if (++s == S) { s = 0; ph ^= 1u; }
     }
   } else if (active_warp) {
@@ -841,8 +867,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
           const int s = chunk_slot(s2, 0u, j, S, &ph);
           const int64_t un = r2 * K + j + S;  // unit that refills the slot
           if (release_slot(L, s, nwarps) && un < n_units)
-            bwd_issue<X, DY, DROT>(p, pl, L, smem, cid + (un >> kshift) * ncl, static_cast<int>(un & (K - 1)), s,
-                                   slice_elt0, rstd_per_row, pol);
+            issue_unit(un, s);
         }
         s2 += K;
         if (s2 >= S) s2 -= S;
@@ -859,9 +884,9 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
 #pragma unroll
   for (int k = 0; k < kVecs; ++k) {
     if ((vmask >> k) & 1u) {
-      if (p.dw_part != nullptr) Vec8<float>::store(p.dw_part + pbase + k * G8, dw[k]);
+      if (p.dw_part != nullptr) Pair8<float>::store(p.dw_part + pbase + k * G8, dw[k]);
       if constexpr (kHasDb) {
-        if (p.db_part != nullptr) Vec8<float>::store(p.db_part + pbase + k * G8, db[kHasDb ? k : 0]);
+        if (p.db_part != nullptr) Pair8<float>::store(p.db_part + pbase + k * G8, db[kHasDb ? k : 0]);
       }
     }
   }
