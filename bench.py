@@ -521,6 +521,7 @@ def main():
     for i in range(args.warmup):
         runners[i % pool].step()
     torch.cuda.synchronize(dev)
+    plan = _lib.last_plan()  # the launch plan of the timed steps (the e2e run below replans)
     # The K timed steps are captured once into a CUDA graph and replayed, so the device
     # time is not diluted by Python/ctypes launch overhead (the library's launches are
     # capturable: no allocation, no synchronisation). The multi-GPU backward keeps eager
@@ -590,7 +591,7 @@ def main():
                 "global_rows": w["rows"] * world, "parallelism": f"dp{world} (row shards, one rank per GPU)",
                 "bytes_per_step_per_rank": algo_bytes(w),
                 "l2": ("inputs larger than L2" if pool == 1 else f"rotating pool of {pool} input sets > L2"),
-                "path": _lib.last_plan(),
+                "path": plan,
                 "timing": "CUDA graph replay of the K steps" if graph is not None else "eager launches",
             },
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
