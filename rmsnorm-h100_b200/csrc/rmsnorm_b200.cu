@@ -452,10 +452,11 @@ using b16 = __nv_bfloat16;
 constexpr int H = RMSNORM_B200_F16, B = RMSNORM_B200_BF16, F = RMSNORM_B200_F32, NA = -1;
 
 // (x, residual, out, residual_out)
-FwdKernel pick_fwd(int x, int r, int o, int ro) {
+FwdKernel pick_fwd(int x, int r, int o, int ro, bool bias) {
 #define RMSB_FWD(XT, XC, RT, RC, OT, OC, ROT, ROC)                              \
   if (x == XC && r == RC && o == OC && ro == ROC)                               \
-    return fwd_stream_kernel<XT, RT, OT, ROT, kMaxVecs, kBlockLarge, 1>;
+    return bias ? fwd_stream_kernel<XT, RT, OT, ROT, true, kMaxVecs, kBlockLarge, 1>  \
+                : fwd_stream_kernel<XT, RT, OT, ROT, false, kMaxVecs, kBlockLarge, 1>;
   RMSB_FWD(b16, B, NoT, NA, b16, B, NoT, NA)
   RMSB_FWD(h16, H, NoT, NA, h16, H, NoT, NA)
   RMSB_FWD(float, F, NoT, NA, float, F, NoT, NA)
@@ -604,7 +605,7 @@ int do_fwd(const rmsnorm_b200_fwd_args* a, cudaStream_t stream) {
       if (p && !aligned16(p)) why = "unaligned pointer";
     if (why.empty()) {
       kernel = pick_fwd(a->x_dtype, a->residual ? a->residual_dtype : NA, a->out_dtype,
-                        a->residual_out ? a->residual_out_dtype : NA);
+                        a->residual_out ? a->residual_out_dtype : NA, a->bias != nullptr);
       if (!kernel) why = "dtype combination";
     }
   }
@@ -893,7 +894,7 @@ extern "C" int rmsnorm_b200_max_active_clusters(int32_t cluster_size, int32_t* c
   DeviceState* ds = nullptr;
   int st = get_device_state(&ds);
   if (st) return st;
-  const void* k = reinterpret_cast<const void*>(pick_fwd(B, NA, B, NA));
+  const void* k = reinterpret_cast<const void*>(pick_fwd(B, NA, B, NA, false));
   if (ensure_attrs(ds, k)) return RMSNORM_B200_ERR_CUDA;
   *clusters = resident_units(ds, k, cluster_size, kSmemOptIn, kBlockLarge);
   return RMSNORM_B200_OK;

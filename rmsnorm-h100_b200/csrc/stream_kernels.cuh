@@ -246,8 +246,9 @@ __device__ __forceinline__ void fwd_issue(const FwdParams& p, const StreamPlan& 
 }
 
 // X: input dtype; RT: residual dtype (NoT = none); OT: output dtype; ROT: residual_out
-// dtype (NoT = not written).
-template <typename X, typename RT, typename OT, typename ROT, int kVecs, int kBlock, int kMinBlocks>
+// dtype (NoT = not written); kBias: a bias is added (without one, its registers and adds
+// are gone: out = h * rstd * w rounds exactly like the fma with a zero bias).
+template <typename X, typename RT, typename OT, typename ROT, bool kBias, int kVecs, int kBlock, int kMinBlocks>
 __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const FwdParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr bool kRes = Present<RT>::value;
@@ -308,15 +309,19 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
 
   // weight / bias of the thread's columns, as float pairs (element 2i in .x, 2i+1 in .y)
   float2 wr[kVecs][4];
-  float2 br[kVecs][4];
+  float2 br[kBias ? kVecs : 1][4];
 #pragma unroll
   for (int k = 0; k < kVecs; ++k) {
     const int64_t c = slice_elt0 + static_cast<int64_t>(gl + k * G) * 8;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) { wr[k][i] = splat2(1.f); br[k][i] = splat2(0.f); }
+    for (int i = 0; i < 4; ++i) wr[k][i] = splat2(1.f);
+    if constexpr (kBias) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) br[kBias ? k : 0][i] = splat2(0.f);
+    }
     if ((vmask >> k) & 1u) {
       if (p.w != nullptr) load8p_rt(p.w, p.w_dt, p.w_per_head ? c : c % pl.N, wr[k]);
-      if (p.b != nullptr) load8p_rt(p.b, p.b_dt, p.b_per_head ? c : c % pl.N, br[k]);
+      if constexpr (kBias) load8p_rt(p.b, p.b_dt, p.b_per_head ? c : c % pl.N, br[kBias ? k : 0]);
     }
   }
   const int xs_stride = static_cast<int>(pl.row_bytes[0] / sizeof(X));  // elements per staged row
@@ -355,7 +360,10 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       if constexpr (kRO) Pair8<ROe>::store(rop, h);
       const float2 r2 = splat2(rstd);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) y[i] = fma2(mul2(h[i], r2), wr[k][i], br[k][i]);
+      for (int i = 0; i < 4; ++i) {
+        if constexpr (kBias) y[i] = fma2(mul2(h[i], r2), wr[k][i], br[kBias ? k : 0][i]);
+        else y[i] = mul2(mul2(h[i], r2), wr[k][i]);
+      }
       Pair8<OT>::store(op, y);
     } else {
       float h[8], r[8], y[8];
@@ -366,8 +374,14 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       if constexpr (kRO) Vec8<ROe>::store(rop, h);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float2 w2 = wr[k][e >> 1], b2 = br[k][e >> 1];
-        y[e] = fmaf(h[e] * rstd, (e & 1) ? w2.y : w2.x, (e & 1) ? b2.y : b2.x);
+        const float2 w2 = wr[k][e >> 1];
+        const float w = (e & 1) ? w2.y : w2.x;
+        if constexpr (kBias) {
+          const float2 b2 = br[kBias ? k : 0][e >> 1];
+          y[e] = fmaf(h[e] * rstd, w, (e & 1) ? b2.y : b2.x);
+        } else {
+          y[e] = (h[e] * rstd) * w;
+        }
       }
       Vec8<OT>::store(op, y);
     }
