@@ -330,7 +330,12 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
   }
   const int rstd_per_row = pl.seg_mode ? H : 1;
   if (rstd_staged) per_row += 4u * rstd_per_row;
-  const int target = env_int("RMSNORM_B200_STAGE_BYTES", 48 * 1024) * T / kBlockLarge;
+  // Tile (stage) size and ring depth, measured on B200: a ring of about 100 KB in at least
+  // two stages streams best (deeper rings delay the first tiles of small problems and gain
+  // nothing on large ones); per-head rows (seg mode) amortise their per-tile work over
+  // bigger tiles.
+  const int dflt_stage = (pl.seg_mode ? (rstd_staged ? 128 : 64) : 48) * 1024;
+  const int target = env_int("RMSNORM_B200_STAGE_BYTES", dflt_stage) * T / kBlockLarge;
   int R = pl.rps;
   if (P == 1) {
     const int64_t m = std::max<int64_t>(1, target / (static_cast<int64_t>(pl.rps) * per_row));
@@ -349,7 +354,7 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
     return off;
   };
   uint32_t stage = layout(R);
-  while (stage > static_cast<uint32_t>(budget) && R > pl.rps) {
+  while (2 * stage > static_cast<uint32_t>(budget) && R > pl.rps) {  // keep two stages
     R -= pl.rps;
     stage = layout(R);
   }
@@ -357,7 +362,9 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
   pl.R = R;
   pl.stage_bytes = stage;
   const int max_s = std::max(1, std::min(kMaxStages, env_int("RMSNORM_B200_MAX_STAGES", kMaxStages)));
-  pl.S = std::max(1, std::min<int>(max_s, budget / static_cast<int>(stage)));
+  const int ring = env_int("RMSNORM_B200_RING_BYTES", 100 * 1024) * T / kBlockLarge;
+  const int s_fit = std::max(1, std::min<int>(max_s, budget / static_cast<int>(stage)));
+  pl.S = std::min(s_fit, std::max(2, ring / static_cast<int>(stage)));
   pl.ntiles = (pl.nrows + R - 1) / R;
   set_prefetch(pl);
   *out = pl;
