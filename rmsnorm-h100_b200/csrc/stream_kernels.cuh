@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
   const bool in_group = gid < pl.rps;
   const int nwarps = (pl.rps * G + 31) >> 5;  // warps with work; the others idle to the end
   const bool active_warp = warp < nwarps;
-  const float n_f = static_cast<float>(pl.N);
+  const float inv_n = 1.f / static_cast<float>(pl.N);  // mean = sum * (1/N), exact for N a power of two
   unsigned vmask = 0;
 #pragma unroll
   for (int k = 0; k < kVecs; ++k)
@@ -466,13 +466,13 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
         float rstd_k[kVecs];
         if (pl.seg_mode) {
 #pragma unroll
-          for (int k = 0; k < kVecs; ++k) rstd_k[k] = rsqrtf(seg_sum(part[k], pl.vs, amask) / n_f + p.eps);
+          for (int k = 0; k < kVecs; ++k) rstd_k[k] = rsqrtf(fmaf(seg_sum(part[k], pl.vs, amask), inv_n, p.eps));
         } else {
           float ss = 0.f;
 #pragma unroll
           for (int k = 0; k < kVecs; ++k) ss += part[k];
           ss = group_sum(ss, pl, L, gid, gl, seq++);
-          const float r = rsqrtf(ss / n_f + p.eps);
+          const float r = rsqrtf(fmaf(ss, inv_n, p.eps));
 #pragma unroll
           for (int k = 0; k < kVecs; ++k) rstd_k[k] = r;
         }
@@ -528,7 +528,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
         const float tot = cluster_recv(pl, L, xc, lane, static_cast<uint32_t>(r2), pre, kSiteFwdCluster);
         const int64_t row = cid + r2 * ncl;
         float rstd_k[kVecs];
-        const float rs = rsqrtf(tot / n_f + p.eps);
+        const float rs = rsqrtf(fmaf(tot, inv_n, p.eps));
 #pragma unroll
         for (int k = 0; k < kVecs; ++k) rstd_k[k] = rs;
         if (in_group) {
@@ -660,7 +660,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   const bool in_group = gid < pl.rps;
   const int nwarps = (pl.rps * G + 31) >> 5;
   const bool active_warp = warp < nwarps;
-  const float n_f = static_cast<float>(pl.N);
+  const float inv_n = 1.f / static_cast<float>(pl.N);  // mean = sum * (1/N), exact for N a power of two
   unsigned vmask = 0;
 #pragma unroll
   for (int k = 0; k < kVecs; ++k)
@@ -817,12 +817,12 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
         pass1(rp, part, rstd_k);
         if (pl.seg_mode) {
 #pragma unroll
-          for (int k = 0; k < kVecs; ++k) c_k[k] = seg_sum(part[k], pl.vs, amask) / n_f;
+          for (int k = 0; k < kVecs; ++k) c_k[k] = seg_sum(part[k], pl.vs, amask) * inv_n;
         } else {
           float dot = 0.f;
 #pragma unroll
           for (int k = 0; k < kVecs; ++k) dot += part[k];
-          const float c = group_sum(dot, pl, L, gid, gl, seq++) / n_f;
+          const float c = group_sum(dot, pl, L, gid, gl, seq++) * inv_n;
 #pragma unroll
           for (int k = 0; k < kVecs; ++k) c_k[k] = c;
         }
@@ -863,7 +863,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
         if (s1 >= S) { s1 -= S; ph1 ^= 1u; }
       }
       if (r2 >= 0 && r2 < n_local) {
-        const float c = cluster_recv(pl, L, xc, lane, static_cast<uint32_t>(r2), pre, kSiteBwdCluster) / n_f;
+        const float c = cluster_recv(pl, L, xc, lane, static_cast<uint32_t>(r2), pre, kSiteBwdCluster) * inv_n;
         const int64_t row = cid + r2 * ncl;
         const RowPtrs rp = row_ptrs(s2, 0);
         if (in_group) {
