@@ -285,6 +285,16 @@ def cpu_step_fn(w, rows):
     return lambda: oracle.bwd(x, wt, dy, rstd, has_bias=w["bias"])
 
 
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_baseline(w, budget_s=10.0):
     torch.set_num_threads(os.cpu_count() or 1)
     rows = cpu_sample_rows(w)
@@ -303,6 +313,7 @@ def cpu_baseline(w, budget_s=10.0):
     per = statistics.median(times)
     gbs = algo_bytes(w, rows) / per / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "cpu_model": cpu_model(), "rows_per_s": round(rows / per, 1),
             "sample": f"{rows} of {w['rows']} rows per step, median of {len(times)} steps, "
                       f"oracle/rmsnorm_oracle.py restating rmsnorm/rmsnorm.py (reference PyTorch CPU path)"}
 
@@ -332,6 +343,7 @@ def run_reference_arm(args, w):
         "data": "synthetic: seeded N(0,1) inputs, weight N(1,0.1), bias N(0,0.02)",
         "config": {"workload": w["desc"], "sample_rows_per_step": rows, "rows": w["rows"], "hidden": w["n"]},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "cpu_model": cpu_model(), "rows_per_s": round(rows / per, 1),
                          "sample": f"{rows} rows per step of the workload; reference PyTorch CPU path restated "
                                    f"in oracle/rmsnorm_oracle.py (reference checkout absent on the GPU box)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -605,6 +617,11 @@ def main():
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
             "gpu_launches": launches,
             "clocks": clk.summary(),
+            # per-config figures of the reference's report: rows/s, per-GPU GB/s, and the
+            # fraction of the nominal HBM roofline (N x 8 TB/s)
+            "rows_per_s": round(w["rows"] * world / (ms_step * 1e-3), 1),
+            "gbs_per_gpu": round(value / world, 2),
+            "frac_of_nominal_8tbs": round(value / (8000.0 * world), 4),
         }
     if group is not None:
         import torch.distributed as dist
