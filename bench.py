@@ -66,6 +66,8 @@ WORKLOADS = {
     "bwd16k": dict(kind="bwd", rows=32768, n=16384, dtype=BF16, bias=False,
                    desc="north-star target backward: RMSNorm backward (32768,16384) bf16, fp32 weight -> dx bf16, "
                         "dweight fp32"),
+    "ln16k": dict(kind="ln", rows=32768, n=16384, dtype=BF16, bias=True,
+                  desc="next-row LayerNorm forward (32768,16384) bf16, fp32 weight+bias, mean and rstd stored"),
     "cfg4f": dict(kind="fwd", rows=16384 * 32, n=128, heads=32, dtype=F16, residual=False, bias=True, ro=None,
                   rstd=True, desc="BASELINE cfg 4 forward: per-head (16384,32,128) fp16, (32,128) fp32 weight+bias, rstd"),
     "cfg4b": dict(kind="bwd", rows=16384 * 32, n=128, heads=32, dtype=F16, bias=True,
@@ -92,6 +94,8 @@ def algo_bytes(w, rows=None):
     e = rows * n
     s = esize(w["dtype"])
     aff = h * n * 4
+    if w["kind"] == "ln":
+        return 2 * e * s + aff * (2 if w["bias"] else 1) + rows * 8
     if w["kind"] == "fwd":
         b = 2 * e * s + aff + (aff if w["bias"] else 0)
         if w["residual"]:
@@ -110,7 +114,7 @@ def algo_bytes(w, rows=None):
 def main_kernel_bytes(w):
     """Bytes of the dominant kernel per launch (the backward's dweight/dbias are written by
     the separate reduction kernel, not by the streaming kernel)."""
-    if w["kind"] == "fwd":
+    if w["kind"] != "bwd":
         return algo_bytes(w)
     h, n = w.get("heads", 1), w["n"]
     return algo_bytes(w) - h * n * 4 * (2 if w["bias"] else 1)
@@ -137,8 +141,8 @@ def make_inputs(w, dev, seed):
     t = {}
     t["x"] = gen(shape, w["dtype"], seed, dev, outliers=w.get("outliers", 0.0))
     t["w"] = gen(aff, F32, seed + 1, dev, "weight")
-    if w["kind"] == "fwd":
-        t["res"] = gen(shape, w["dtype"], seed + 2, dev) if w["residual"] else None
+    if w["kind"] in ("fwd", "ln"):
+        t["res"] = gen(shape, w["dtype"], seed + 2, dev) if w.get("residual") else None
         t["b"] = gen(aff, F32, seed + 3, dev, "bias") if w["bias"] else None
     else:
         t["dy"] = gen(shape, w["dtype"], seed + 4, dev)
@@ -161,7 +165,11 @@ class Runner:
         self.w, self.t, self.dev, self.group, self.lib = w, t, dev, group, _lib
         h = w.get("heads", 1)
         x = t["x"]
-        if w["kind"] == "fwd":
+        if w["kind"] == "ln":
+            self.out = torch.empty_like(x)
+            self.mean = torch.empty(x.shape[0], dtype=F32, device=dev)
+            self.rstd = torch.empty(x.shape[0], dtype=F32, device=dev)
+        elif w["kind"] == "fwd":
             self.out = torch.empty_like(x)
             self.ro = torch.empty(x.shape, dtype=w["ro"], device=dev) if w["ro"] is not None else None
             self.rstd = torch.empty(x.shape[0], dtype=F32, device=dev) if w["rstd"] else None
@@ -176,7 +184,9 @@ class Runner:
     def step(self):
         w, t = self.w, self.t
         h = w.get("heads", 1)
-        if w["kind"] == "fwd":
+        if w["kind"] == "ln":
+            self.lib.layernorm_fwd(t["x"], w["n"], t["w"], t["b"], self.out, self.mean, self.rstd, 1e-6)
+        elif w["kind"] == "fwd":
             self.lib.fwd(t["x"], t["res"], t["w"], h, t["b"], h, self.out, self.ro, self.rstd, h, 1e-6)
         else:
             self.lib.bwd(self.args, self.dev, self.ws)
@@ -276,6 +286,9 @@ def cpu_step_fn(w, rows):
     wt = gen(aff, F32, 2, "cpu", "weight")
     if h > 1:
         x = x.reshape(rows // h, h, w["n"])
+    if w["kind"] == "ln":
+        b = gen(aff, F32, 4, "cpu", "bias") if w["bias"] else None
+        return lambda: oracle.layernorm_fwd(x, wt, b)
     if w["kind"] == "fwd":
         res = gen(x.shape, w["dtype"], 3, "cpu") if w["residual"] else None
         b = gen(aff, F32, 4, "cpu", "bias") if w["bias"] else None
@@ -357,6 +370,10 @@ def run_refgpu(args, w):
     GPU, device time of K steps (CUDA graph replay when capturable, else eager)."""
     from oracle import ref_gpu
 
+    if w["kind"] == "ln":
+        print(json.dumps({"impl": "refgpu", "unavailable": "the reference has no LayerNorm kernel (its "
+                          "layernorm_fwd is PyTorch ops)"}), flush=True)
+        return
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     ext = ref_gpu.load()
@@ -415,7 +432,19 @@ def e2e_measure(w, t_dev, dev, steps, group):
     wt, b = t_dev["w"], t_dev.get("b")
     stream = torch.cuda.current_stream(dev)
     rows, n = w["rows"], w["n"]
-    if w["kind"] == "fwd":
+    if w["kind"] == "ln":
+        out_h = torch.empty((rows, n), dtype=w["dtype"], pin_memory=True)
+        mean = torch.empty(rows, dtype=F32, device=dev)
+        rstd = torch.empty(rows, dtype=F32, device=dev)
+        stats_h = torch.empty(2, rows, dtype=F32, pin_memory=True)
+
+        def one():
+            pipe.layernorm(host["x"], wt, b, out=out_h, mean=mean, rstd=rstd)
+            stats_h[0].copy_(mean, non_blocking=True)
+            stats_h[1].copy_(rstd, non_blocking=True)
+
+        d2h = out_h.numel() * out_h.element_size() + rows * 8
+    elif w["kind"] == "fwd":
         out_h = torch.empty((rows, n), dtype=w["dtype"], pin_memory=True)
         ro_h = torch.empty((rows, n), dtype=w["ro"], pin_memory=True) if w["ro"] is not None else None
         rstd = torch.empty(rows, dtype=F32, device=dev) if w["rstd"] else None

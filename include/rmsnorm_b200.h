@@ -155,6 +155,29 @@ int rmsnorm_b200_bwd(const rmsnorm_b200_bwd_args* args, void* workspace, size_t 
 #define RMSNORM_B200_NOALLOC_SCRATCH_BYTES (16u << 20)
 int rmsnorm_b200_bwd_noalloc(const rmsnorm_b200_bwd_args* args, void* stream);
 
+/* LayerNorm forward over rows of `hidden` elements: mean, variance as the mean of squared
+ * deviations (fp32), out = (x - mean) * rsqrt(var + eps) * weight + bias. Replaces the
+ * PyTorch implementation of layernorm_fwd (rmsnorm/rmsnorm.py:655-676); the reference has
+ * no native kernel for it. */
+typedef struct rmsnorm_b200_ln_fwd_args {
+  int64_t rows;               /* >= 0 */
+  int64_t hidden;             /* >= 1 (the normalised size) */
+  int32_t x_dtype;
+  int32_t weight_dtype;
+  const void* x;              /* [rows, hidden] */
+  const void* weight;         /* nullable (ones), [hidden] */
+  const void* bias;           /* nullable (zeros), [hidden] */
+  int32_t bias_dtype;
+  int32_t out_dtype;
+  void* out;                  /* nullable (statistics only), [rows, hidden] */
+  float* mean;                /* nullable, [rows] fp32 */
+  float* rstd;                /* nullable, [rows] fp32 */
+  float eps;
+  int32_t reserved0;
+} rmsnorm_b200_ln_fwd_args;
+
+int rmsnorm_b200_layernorm_fwd(const rmsnorm_b200_ln_fwd_args* args, void* stream);
+
 /* Static, human-readable message for a status code. */
 const char* rmsnorm_b200_strerror(int status);
 

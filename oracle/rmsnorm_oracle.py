@@ -112,6 +112,20 @@ def fwd_rows_chunked(x, weight=None, bias=None, residual=None, eps=1e-6, rows=No
     return (torch.cat(outs), torch.cat(ros) if ros else None, torch.cat(rstds), torch.cat(ys))
 
 
+def layernorm_fwd(x: Tensor, weight: Tensor, bias: Optional[Tensor] = None, eps: float = 1e-6):
+    """LayerNorm forward restating rmsnorm/rmsnorm.py:655-676 in fp32 on the host: out =
+    layer_norm over weight's shape (x.dtype); mean and rstd over the last dim (fp32).
+    Returns (out, rstd, mean, y_f32) with y_f32 the fp32 output before the final cast."""
+    xf = x.float()
+    y = torch.nn.functional.layer_norm(
+        xf, weight.shape, weight.float(), bias.float() if bias is not None else None, eps
+    )
+    mean = xf.mean(dim=-1)
+    var = ((xf - mean.unsqueeze(-1)) ** 2).mean(dim=-1)
+    rstd = torch.rsqrt(var + eps)
+    return y.to(x.dtype), rstd, mean, y
+
+
 # ---------------------------------------------------------------------------------------
 # Seeded inputs with the BASELINE distributions (x, dy, residual ~ N(0,1); weight ~ N(1, 0.1);
 # bias ~ N(0, 0.02); optional 1% element outliers x100). Generated on the host with a

@@ -75,6 +75,50 @@ __global__ void __launch_bounds__(kGenericThreads) fwd_generic_kernel(const GenF
   }
 }
 
+// LayerNorm forward, generic path: mean, then the mean of squared deviations (two passes,
+// so the variance has no cancellation), then out = (x - mean) * rstd * w + b. `out` may be
+// null (statistics only); w null = ones, b null = zeros.
+struct GenLnParams {
+  int64_t rows, N;
+  const void* x; int32_t x_dt;
+  const void* w; int32_t w_dt;
+  const void* b; int32_t b_dt;
+  void* out; int32_t out_dt;
+  float* mean;
+  float* rstd;
+  float eps;
+};
+
+__global__ void __launch_bounds__(kGenericThreads) ln_generic_kernel(const GenLnParams p) {
+  __shared__ float red[32];
+  const int64_t N = p.N;
+  const float inv_n = 1.f / static_cast<float>(N);
+  for (int64_t r = blockIdx.x; r < p.rows; r += gridDim.x) {
+    const int64_t base = r * N;
+    float acc = 0.f;
+    for (int64_t n = threadIdx.x; n < N; n += blockDim.x) acc += load1_rt(p.x, p.x_dt, base + n);
+    const float mean = block_sum_fixed(acc, red) * inv_n;
+    acc = 0.f;
+    for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+      const float d = load1_rt(p.x, p.x_dt, base + n) - mean;
+      acc = fmaf(d, d, acc);
+    }
+    const float rs = rsqrtf(fmaf(block_sum_fixed(acc, red), inv_n, p.eps));
+    if (p.out) {
+      for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+        const float d = load1_rt(p.x, p.x_dt, base + n) - mean;
+        const float w = p.w ? load1_rt(p.w, p.w_dt, n) : 1.f;
+        const float b = p.b ? load1_rt(p.b, p.b_dt, n) : 0.f;
+        store1_rt(p.out, p.out_dt, base + n, fmaf(d * rs, w, b));
+      }
+    }
+    if (threadIdx.x == 0) {
+      if (p.mean) p.mean[r] = mean;
+      if (p.rstd) p.rstd[r] = rs;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kGenericThreads) bwd_generic_dx_kernel(const GenBwdParams p) {
   __shared__ float red[32];
   const int64_t N = p.N;

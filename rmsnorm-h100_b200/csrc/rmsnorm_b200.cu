@@ -462,8 +462,8 @@ constexpr int H = RMSNORM_B200_F16, B = RMSNORM_B200_BF16, F = RMSNORM_B200_F32,
 FwdKernel pick_fwd(int x, int r, int o, int ro, bool bias) {
 #define RMSB_FWD(XT, XC, RT, RC, OT, OC, ROT, ROC)                              \
   if (x == XC && r == RC && o == OC && ro == ROC)                               \
-    return bias ? fwd_stream_kernel<XT, RT, OT, ROT, true, kMaxVecs, kBlockLarge, 1>  \
-                : fwd_stream_kernel<XT, RT, OT, ROT, false, kMaxVecs, kBlockLarge, 1>;
+    return bias ? fwd_stream_kernel<XT, RT, OT, ROT, true, false, kMaxVecs, kBlockLarge, 1>  \
+                : fwd_stream_kernel<XT, RT, OT, ROT, false, false, kMaxVecs, kBlockLarge, 1>;
   RMSB_FWD(b16, B, NoT, NA, b16, B, NoT, NA)
   RMSB_FWD(h16, H, NoT, NA, h16, H, NoT, NA)
   RMSB_FWD(float, F, NoT, NA, float, F, NoT, NA)
@@ -478,6 +478,20 @@ FwdKernel pick_fwd(int x, int r, int o, int ro, bool bias) {
   RMSB_FWD(b16, B, NoT, NA, float, F, NoT, NA)
   RMSB_FWD(h16, H, NoT, NA, float, F, NoT, NA)
 #undef RMSB_FWD
+  return nullptr;
+}
+
+// LayerNorm: x and out of one dtype, no residual.
+FwdKernel pick_ln(int x, int o, bool bias) {
+  if (x != o) return nullptr;
+#define RMSB_LN(XT, XC)                                                                              \
+  if (x == XC)                                                                                       \
+    return bias ? fwd_stream_kernel<XT, NoT, XT, NoT, true, true, kMaxVecs, kBlockLarge, 1>          \
+                : fwd_stream_kernel<XT, NoT, XT, NoT, false, true, kMaxVecs, kBlockLarge, 1>;
+  RMSB_LN(b16, B)
+  RMSB_LN(h16, H)
+  RMSB_LN(float, F)
+#undef RMSB_LN
   return nullptr;
 }
 
@@ -634,6 +648,75 @@ int do_fwd(const rmsnorm_b200_fwd_args* a, cudaStream_t stream) {
     }
   }
   return launch_fwd_generic(ds, a, stream, why);
+}
+
+// ---------------------------------------------------------------------------------------
+// LayerNorm forward
+// ---------------------------------------------------------------------------------------
+int check_ln(const rmsnorm_b200_ln_fwd_args* a) {
+  if (!a) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  int st = check_common(a->rows, a->hidden, 1);
+  if (st) return st;
+  if (!valid_dt(a->x_dtype)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->rows > 0 && !a->x) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->out && !valid_dt(a->out_dtype)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->weight && !valid_dt(a->weight_dtype)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  if (a->bias && !valid_dt(a->bias_dtype)) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  return RMSNORM_B200_OK;
+}
+
+int do_ln(const rmsnorm_b200_ln_fwd_args* a, cudaStream_t stream) {
+  int st = check_ln(a);
+  if (st) return st;
+  if (a->rows == 0) { t_last_plan = "ln empty"; return RMSNORM_B200_OK; }
+  DeviceState* ds = nullptr;
+  st = get_device_state(&ds);
+  if (st) return st;
+  std::string why;
+  FwdKernel kernel = nullptr;
+  if (env_int("RMSNORM_B200_FORCE_GENERIC", 0)) {
+    why = "forced";
+  } else if (a->hidden % 8) {
+    why = "hidden % 8";
+  } else if (!a->out) {
+    why = "statistics only";
+  } else {
+    const void* ptrs[] = {a->x, a->weight, a->bias, a->out};
+    for (const void* p : ptrs)
+      if (p && !aligned16(p)) why = "unaligned pointer";
+    if (why.empty()) {
+      kernel = pick_ln(a->x_dtype, a->out_dtype, a->bias != nullptr);
+      if (!kernel) why = "dtype combination";
+    }
+  }
+  if (kernel) {
+    StreamPlan pl;
+    const int in_bytes[3] = {elem_bytes(a->x_dtype), 0, 0};
+    // rows are never split across CTAs: a row that does not fit one CTA takes the generic path
+    if (make_stream_plan(a->rows, a->hidden, 1, in_bytes, false, kMaxVecs, kLarge, 1, &pl, &why)) {
+      FwdParams p = {};
+      p.x = a->x; p.w = a->weight; p.b = a->bias; p.out = a->out;
+      p.rstd = a->rstd; p.mean = a->mean;
+      p.w_dt = a->weight_dtype; p.b_dt = a->bias_dtype;
+      p.eps = a->eps;
+      st = launch_stream(ds, kernel, p, pl, stream, "ln_stream", false, nullptr);
+      if (st != RMSNORM_B200_ERR_UNSUPPORTED) return st;
+      why = "not schedulable";
+    }
+  }
+  GenLnParams g = {};
+  g.rows = a->rows; g.N = a->hidden;
+  g.x = a->x; g.x_dt = a->x_dtype;
+  g.w = a->weight; g.w_dt = a->weight_dtype;
+  g.b = a->bias; g.b_dt = a->bias_dtype;
+  g.out = a->out; g.out_dt = a->out_dtype;
+  g.mean = a->mean; g.rstd = a->rstd; g.eps = a->eps;
+  const int64_t grid = std::min<int64_t>(a->rows, static_cast<int64_t>(ds->sm_count) * 8);
+  ln_generic_kernel<<<static_cast<unsigned>(grid), kGenericThreads, 0, stream>>>(g);
+  if (cudaGetLastError() != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  t_last_plan = "ln_generic (" + why + ") grid=" + std::to_string(grid);
+  return RMSNORM_B200_OK;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -812,6 +895,10 @@ using namespace rmsb200;
 
 extern "C" int rmsnorm_b200_fwd(const rmsnorm_b200_fwd_args* args, void* stream) {
   return do_fwd(args, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int rmsnorm_b200_layernorm_fwd(const rmsnorm_b200_ln_fwd_args* args, void* stream) {
+  return do_ln(args, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int rmsnorm_b200_bwd_workspace_size(const rmsnorm_b200_bwd_args* args, size_t* bytes) {

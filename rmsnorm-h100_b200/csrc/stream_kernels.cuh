@@ -247,8 +247,11 @@ __device__ __forceinline__ void fwd_issue(const FwdParams& p, const StreamPlan& 
 
 // X: input dtype; RT: residual dtype (NoT = none); OT: output dtype; ROT: residual_out
 // dtype (NoT = not written); kBias: a bias is added (without one, its registers and adds
-// are gone: out = h * rstd * w rounds exactly like the fma with a zero bias).
-template <typename X, typename RT, typename OT, typename ROT, bool kBias, int kVecs, int kBlock, int kMinBlocks>
+// are gone: out = h * rstd * w rounds exactly like the fma with a zero bias); kLN:
+// LayerNorm instead of RMSNorm (no residual; mean, then the mean of squared deviations
+// from the staged tile, out = (x - mean) * rstd * w + b; rows are never split).
+template <typename X, typename RT, typename OT, typename ROT, bool kBias, bool kLN, int kVecs, int kBlock,
+          int kMinBlocks>
 __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const FwdParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr bool kRes = Present<RT>::value;
@@ -406,6 +409,38 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
   auto stage_r = [&](int s) {
     return reinterpret_cast<const RTe*>(smem + static_cast<size_t>(s) * pl.stage_bytes + pl.off[1]) + gl * 8;
   };
+  // LayerNorm per-vector passes: sum, sum of squared deviations from the mean, output
+  auto ln_sum = [&](const X* xp) {
+    float2 h[4];
+    Pair8<X>::load(xp, h);
+    const float2 a = add2(add2(h[0], h[1]), add2(h[2], h[3]));
+    return a.x + a.y;
+  };
+  auto ln_dev = [&](const X* xp, float mean) {
+    float2 h[4];
+    Pair8<X>::load(xp, h);
+    const float2 nm = splat2(-mean);
+    float2 d = add2(h[0], nm);
+    float2 a = mul2(d, d);
+#pragma unroll
+    for (int i = 1; i < 4; ++i) {
+      d = add2(h[i], nm);
+      a = fma2(d, d, a);
+    }
+    return a.x + a.y;
+  };
+  auto ln_emit = [&](const X* xp, OT* op, float mean, float rstd, int k) {
+    float2 h[4], y[4];
+    Pair8<X>::load(xp, h);
+    const float2 nm = splat2(-mean), r2 = splat2(rstd);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 xh = mul2(add2(h[i], nm), r2);
+      if constexpr (kBias) y[i] = fma2(xh, wr[k][i], br[kBias ? k : 0][i]);
+      else y[i] = mul2(xh, wr[k][i]);
+    }
+    Pair8<OT>::store(op, y);
+  };
   // the same two passes over a split row held as K > 1 chunks, first chunk in slot sb
   const int kpc_shift = pl.kpc_shift;
   const int kpc_mask = (1 << kpc_shift) - 1;
@@ -462,39 +497,76 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
         const RTe* rs = rs0 + lr * xs_stride;
         const int64_t row = row0 + lr;
         float part[kVecs];
-        pass1(xs, rs, part);
         float rstd_k[kVecs];
-        if (pl.seg_mode) {
+        float mean_k[kVecs];
+        // segment (seg mode) or row-group (row mode) sum of part[], scaled by `scale`
+        auto reduce_k = [&](const float (&pt)[kVecs], float (&res)[kVecs], float scale) {
+          if (pl.seg_mode) {
 #pragma unroll
-          for (int k = 0; k < kVecs; ++k) rstd_k[k] = rsqrtf(fmaf(seg_sum(part[k], pl.vs, amask), inv_n, p.eps));
+            for (int k = 0; k < kVecs; ++k) res[k] = seg_sum(pt[k], pl.vs, amask) * scale;
+          } else {
+            float t = 0.f;
+#pragma unroll
+            for (int k = 0; k < kVecs; ++k) t += pt[k];
+            t = group_sum(t, pl, L, gid, gl, seq++) * scale;
+#pragma unroll
+            for (int k = 0; k < kVecs; ++k) res[k] = t;
+          }
+        };
+        if constexpr (kLN) {
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) part[k] = ((vmask >> k) & 1u) ? ln_sum(xs + k * G8) : 0.f;
+          reduce_k(part, mean_k, inv_n);
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) part[k] = ((vmask >> k) & 1u) ? ln_dev(xs + k * G8, mean_k[k]) : 0.f;
+          reduce_k(part, rstd_k, inv_n);
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) rstd_k[k] = rsqrtf(rstd_k[k] + p.eps);
+          if (p.out != nullptr) {
+            OT* op = static_cast<OT*>(p.out) + row * pl.W + gl * 8;
+#pragma unroll
+            for (int k = 0; k < kVecs; ++k)
+              if ((vmask >> k) & 1u) ln_emit(xs + k * G8, op + k * G8, mean_k[k], rstd_k[k], k);
+          }
         } else {
-          float ss = 0.f;
+          pass1(xs, rs, part);
+          if (pl.seg_mode) {
 #pragma unroll
-          for (int k = 0; k < kVecs; ++k) ss += part[k];
-          ss = group_sum(ss, pl, L, gid, gl, seq++);
-          const float r = rsqrtf(fmaf(ss, inv_n, p.eps));
+            for (int k = 0; k < kVecs; ++k)
+              rstd_k[k] = rsqrtf(fmaf(seg_sum(part[k], pl.vs, amask), inv_n, p.eps));
+          } else {
+            float ss = 0.f;
 #pragma unroll
-          for (int k = 0; k < kVecs; ++k) rstd_k[k] = r;
+            for (int k = 0; k < kVecs; ++k) ss += part[k];
+            ss = group_sum(ss, pl, L, gid, gl, seq++);
+            const float r = rsqrtf(fmaf(ss, inv_n, p.eps));
+#pragma unroll
+            for (int k = 0; k < kVecs; ++k) rstd_k[k] = r;
+          }
+          pass2(xs, rs, row, rstd_k);
         }
-        pass2(xs, rs, row, rstd_k);
-        if (p.rstd != nullptr) {
+        // per-row (per-segment) statistics: one lane of each segment or row group stores
+        auto store_stat = [&](float* dst, const float (&v_k)[kVecs]) {
           if (pl.seg_mode) {
 #pragma unroll
             for (int k = 0; k < kVecs; ++k) {
               const int v = gl + k * G;
-              if (((vmask >> k) & 1u) && (v & (pl.vs - 1)) == 0)
-                p.rstd[row * pl.heads + (v >> pl.vs_shift)] = rstd_k[k];
+              if (((vmask >> k) & 1u) && (v & (pl.vs - 1)) == 0) dst[row * pl.heads + (v >> pl.vs_shift)] = v_k[k];
             }
           } else if (gl == 0) {
-            p.rstd[row] = rstd_k[0];
+            dst[row] = v_k[0];
           }
+        };
+        if (p.rstd != nullptr) store_stat(p.rstd, rstd_k);
+        if constexpr (kLN) {
+          if (p.mean != nullptr) store_stat(p.mean, mean_k);
         }
       }
       if (release_slot(L, s, nwarps) && q + S < n_local)
         issue_unit(q + S, s);
       if (++s == S) { s = 0; ph ^= 1u; }
     }
-  } else if (active_warp) {
+  } else if (active_warp && !kLN) {
     // --------- split-row loop (rows split over the cluster, one row per tile) ---------
     // Iteration i: pass 1 of row i and its exchange, then pass 2 of row i - lag.
     const int lag = pl.lag;

@@ -79,6 +79,7 @@ struct FwdParams {
   int32_t w_dt, b_dt;
   int32_t w_per_head, b_per_head;  // 1 when the affine tensor is [H, N]
   float eps;
+  float* mean;     // LayerNorm: per-row mean (null = not stored)
   XRecord* xrec;   // kXGlobal: this launch's record set ([kXRecMaxCtas][kXSlots])
   uint32_t xepoch; // kXGlobal: launch epoch (never 0 modulo 2^31)
 };

@@ -82,8 +82,28 @@ class BwdArgs(ctypes.Structure):
 
 
 # Every symbol include/rmsnorm_b200.h declares, with (restype, argtypes).
+class LnFwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("rows", ctypes.c_int64),
+        ("hidden", ctypes.c_int64),
+        ("x_dtype", ctypes.c_int32),
+        ("weight_dtype", ctypes.c_int32),
+        ("x", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("bias_dtype", ctypes.c_int32),
+        ("out_dtype", ctypes.c_int32),
+        ("out", ctypes.c_void_p),
+        ("mean", ctypes.c_void_p),
+        ("rstd", ctypes.c_void_p),
+        ("eps", ctypes.c_float),
+        ("reserved0", ctypes.c_int32),
+    ]
+
+
 SIGNATURES = {
     "rmsnorm_b200_fwd": (ctypes.c_int, [ctypes.POINTER(FwdArgs), ctypes.c_void_p]),
+    "rmsnorm_b200_layernorm_fwd": (ctypes.c_int, [ctypes.POINTER(LnFwdArgs), ctypes.c_void_p]),
     "rmsnorm_b200_bwd_workspace_size": (
         ctypes.c_int,
         [ctypes.POINTER(BwdArgs), ctypes.POINTER(ctypes.c_size_t)],
@@ -211,6 +231,42 @@ def fwd(
     a.eps = eps
     with torch.cuda.device(x.device):
         _check(lib.rmsnorm_b200_fwd(ctypes.byref(a), _stream_handle(x.device)), "rmsnorm_b200_fwd")
+
+
+def layernorm_fwd(
+    x: torch.Tensor,
+    hidden: int,
+    weight: Optional[torch.Tensor],
+    bias: Optional[torch.Tensor],
+    out: Optional[torch.Tensor],
+    mean: Optional[torch.Tensor],
+    rstd: Optional[torch.Tensor],
+    eps: float,
+) -> None:
+    """Enqueues the LayerNorm forward on the current stream of x's device over rows of
+    `hidden` elements of the contiguous x (out null = statistics only)."""
+    lib = load_library()
+    a = LnFwdArgs()
+    a.rows = x.numel() // hidden if hidden else 0
+    a.hidden = hidden
+    a.x_dtype = _DTYPE_CODES[x.dtype]
+    a.x = x.data_ptr()
+    if weight is not None:
+        a.weight = weight.data_ptr()
+        a.weight_dtype = _DTYPE_CODES[weight.dtype]
+    if bias is not None:
+        a.bias = bias.data_ptr()
+        a.bias_dtype = _DTYPE_CODES[bias.dtype]
+    if out is not None:
+        a.out = out.data_ptr()
+        a.out_dtype = _DTYPE_CODES[out.dtype]
+    if mean is not None:
+        a.mean = mean.data_ptr()
+    if rstd is not None:
+        a.rstd = rstd.data_ptr()
+    a.eps = eps
+    with torch.cuda.device(x.device):
+        _check(lib.rmsnorm_b200_layernorm_fwd(ctypes.byref(a), _stream_handle(x.device)), "rmsnorm_b200_layernorm_fwd")
 
 
 def bwd_args(

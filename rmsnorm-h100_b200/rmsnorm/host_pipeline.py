@@ -120,6 +120,29 @@ class HostPipeline:
         self._run(rows, ins, outs, launch, multiple=h)
         return out, residual_out
 
+    def layernorm(self, x: torch.Tensor, weight: Optional[torch.Tensor], bias: Optional[torch.Tensor] = None,
+                  eps: float = 1e-6, out: Optional[torch.Tensor] = None, mean: Optional[torch.Tensor] = None,
+                  rstd: Optional[torch.Tensor] = None):
+        """LayerNorm forward of a host tensor x ([rows, N], pinned for overlap) with device
+        weight / bias (N,). Returns out on the host; `mean` / `rstd` (device fp32, one per
+        row) are filled when given."""
+        rows, n = x.shape
+        if out is None:
+            out = torch.empty((rows, n), dtype=x.dtype, pin_memory=True)
+        w = weight.contiguous() if weight is not None else None
+        b = bias.contiguous() if bias is not None else None
+        state = {"row": 0}
+
+        def launch(buf, m):
+            r0 = state["row"]
+            _lib.layernorm_fwd(buf["x"][:m], n, w, b, buf["out"][:m],
+                               mean[r0:r0 + m] if mean is not None else None,
+                               rstd[r0:r0 + m] if rstd is not None else None, float(eps))
+            state["row"] = r0 + m
+
+        self._run(rows, {"x": x}, {"out": out}, launch, multiple=1)
+        return out
+
     def bwd(self, x: torch.Tensor, weight: Optional[torch.Tensor], dout: torch.Tensor, rstd: torch.Tensor,
             has_bias: bool = False, dx: Optional[torch.Tensor] = None):
         """Backward of host tensors x / dout ([rows, N], pinned) with device weight and

@@ -371,13 +371,66 @@ class QuackRMSNorm(torch.nn.RMSNorm):
 
 
 # ---------------------------------------------------------------------------------------
-# LayerNorm helpers: pure PyTorch in the reference too (rmsnorm/rmsnorm.py:651-686);
-# re-exported for API compatibility, not part of the accelerated path.
+# LayerNorm. The reference computes these with PyTorch ops (rmsnorm/rmsnorm.py:651-686);
+# here layernorm_fwd on CUDA tensors runs the library's LayerNorm kernels. The *_ref
+# helpers stay the reference's PyTorch formulas.
 # ---------------------------------------------------------------------------------------
 layernorm_ref = _host.layernorm_ref
-layernorm_fwd = _host.layernorm_fwd
 layernorm_rstd_ref = _host.layernorm_rstd_ref
 layernorm_mean_ref = _host.layernorm_mean_ref
+
+_LN_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
+
+
+def layernorm_fwd(
+    x: Tensor,
+    weight: Tensor,
+    bias: Optional[Tensor] = None,
+    eps: float = 1e-6,
+    return_rstd: bool = False,
+    return_mean: bool = False,
+):
+    """LayerNorm forward (rmsnorm/rmsnorm.py:655-676): `out` normalises over weight's shape
+    (the trailing weight.dim() dimensions of x, as torch.nn.functional.layer_norm does) and
+    is returned in x.dtype; `rstd` and `mean` (fp32) are over the last dimension, as the
+    reference returns them. Returns out, (out, rstd), (out, mean) or (out, rstd, mean)."""
+    if not x.is_cuda:
+        return _host.layernorm_fwd(x, weight, bias, eps, return_rstd, return_mean)
+    nshape = tuple(weight.shape)
+    if x.dim() < len(nshape) or tuple(x.shape[x.dim() - len(nshape):]) != nshape:
+        raise RuntimeError(
+            f"Given normalized_shape={list(nshape)}, expected input with shape "
+            f"[*, {', '.join(str(d) for d in nshape)}], but got input of size{list(x.shape)}"
+        )
+    if bias is not None and tuple(bias.shape) != nshape:
+        raise RuntimeError(f"Expected bias to be of same shape as normalized_shape, but got bias of shape "
+                           f"{list(bias.shape)} and normalized_shape = {list(nshape)}")
+    for t in (weight, bias):
+        if t is not None and t.device != x.device:
+            raise RuntimeError("Expected all tensors to be on the same device")
+    if x.dtype not in _LN_DTYPES or weight.dtype not in _LN_DTYPES or (bias is not None and bias.dtype not in _LN_DTYPES):
+        raise TypeError("layernorm_fwd supports float16, bfloat16 and float32 tensors on CUDA")
+    xc = x.contiguous()
+    out = torch.empty_like(xc)
+    need_stats = return_rstd or return_mean
+    mean = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device) if need_stats else None
+    rstd = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device) if return_rstd else None
+    if x.numel() > 0:
+        w = weight.contiguous()
+        b = bias.contiguous() if bias is not None else None
+        if weight.dim() == 1:
+            _lib.layernorm_fwd(xc, x.shape[-1], w, b, out, mean, rstd, eps)
+        else:
+            _lib.layernorm_fwd(xc, weight.numel(), w, b, out, None, None, eps)
+            if need_stats:
+                _lib.layernorm_fwd(xc, x.shape[-1], None, None, None, mean, rstd, eps)
+    if return_rstd and return_mean:
+        return out, rstd, mean
+    if return_rstd:
+        return out, rstd
+    if return_mean:
+        return out, mean
+    return out
 
 rmsnorm_fwd_tuned = rmsnorm_fwd
 rmsnorm_bwd_tuned = rmsnorm_bwd

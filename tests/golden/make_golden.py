@@ -150,7 +150,29 @@ def main(ref_root: str) -> None:
     dx, dw, db, dres = ref.rmsnorm_bwd(x, w, dy, rstd, has_bias=True, bias=b)
     save("sem_perhead_mixed_bias", {"eps": eps}, {"x": x, "weight": w, "bias": b, "dout": dy, "rstd": rstd,
                                                   "dx": dx, "dweight": dw, "dbias": db})
+    make_layernorm(ref, eps)
     print("golden vectors written to", HERE)
+
+
+def make_layernorm(ref, eps: float) -> None:
+    """LayerNorm forward (rmsnorm/rmsnorm.py:655-676) through the reference's layernorm_fwd."""
+    x = gen((16, 1024), torch.bfloat16, 40)
+    w = gen((1024,), torch.float32, 41, "weight")
+    b = gen((1024,), torch.float32, 42, "bias")
+    out, rstd, mean = ref.layernorm_fwd(x, w, bias=b, eps=eps, return_rstd=True, return_mean=True)
+    save("ln_fwd_bf16", {"eps": eps}, {"x": x, "weight": w, "bias": b, "out": out, "rstd": rstd, "mean": mean})
+
+    # 2-D weight: out normalised over the last two dims, rstd / mean over the last dim
+    x = gen((8, 4, 64), torch.float16, 43)
+    w = gen((4, 64), torch.float32, 44, "weight")
+    out, rstd, mean = ref.layernorm_fwd(x, w, eps=eps, return_rstd=True, return_mean=True)
+    save("ln_fwd_2d_weight", {"eps": eps}, {"x": x, "weight": w, "out": out, "rstd": rstd, "mean": mean})
+
+    # fp32 rows of 100 (not a multiple of 8), 1% x100 outliers, rstd only
+    x = gen((8, 100), torch.float32, 45, outliers=0.01)
+    w = gen((100,), torch.float32, 46, "weight")
+    out, rstd = ref.layernorm_fwd(x, w, eps=eps, return_rstd=True)
+    save("ln_fwd_f32_n100", {"eps": eps}, {"x": x, "weight": w, "out": out, "rstd": rstd})
 
 
 if __name__ == "__main__":

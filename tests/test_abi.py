@@ -43,7 +43,8 @@ def _c_layout(struct_name, fields):
 
 
 @pytest.mark.parametrize("cls,cname", [(_lib.FwdArgs, "rmsnorm_b200_fwd_args"),
-                                       (_lib.BwdArgs, "rmsnorm_b200_bwd_args")])
+                                       (_lib.BwdArgs, "rmsnorm_b200_bwd_args"),
+                                       (_lib.LnFwdArgs, "rmsnorm_b200_ln_fwd_args")])
 def test_ctypes_struct_layout_matches_c(cls, cname, tmp_path):
     fields = [f[0] for f in cls._fields_]
     c = tmp_path / "probe.c"
@@ -70,6 +71,12 @@ def test_invalid_arguments_return_status_codes():
     # zero rows: valid and a no-op (no device needed)
     a = _lib.FwdArgs(rows=0, hidden=16, heads=1, x=0x1000, out=0x2000)
     assert lib.rmsnorm_b200_fwd(ctypes.byref(a), None) == 0
+    ln = _lib.LnFwdArgs(rows=4, hidden=16, x=0x1000, out=0x2000, x_dtype=9)
+    assert lib.rmsnorm_b200_layernorm_fwd(ctypes.byref(ln), None) == 1
+    ln = _lib.LnFwdArgs(rows=4, hidden=0, x=0x1000)
+    assert lib.rmsnorm_b200_layernorm_fwd(ctypes.byref(ln), None) == 1
+    ln = _lib.LnFwdArgs(rows=0, hidden=16, x=0x1000)
+    assert lib.rmsnorm_b200_layernorm_fwd(ctypes.byref(ln), None) == 0
     b = _lib.BwdArgs(rows=4, hidden=16, heads=1)  # null pointers
     assert lib.rmsnorm_b200_bwd(ctypes.byref(b), None, 0, None) == 1
     n = ctypes.c_size_t(123)

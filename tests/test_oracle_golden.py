@@ -157,3 +157,27 @@ def test_package_host_path_reproduces_reference_autograd():
     assert torch.equal(x.grad, g["dx"])
     assert torch.allclose(w.grad, g["dweight"], rtol=1e-6, atol=1e-6)
     assert torch.allclose(b.grad, g["dbias"], rtol=1e-6, atol=1e-6)
+
+
+LN_CASES = ["ln_fwd_bf16", "ln_fwd_2d_weight", "ln_fwd_f32_n100"]
+
+
+@pytest.mark.parametrize("name", LN_CASES)
+def test_torch_oracle_layernorm_matches_reference(name):
+    """The LayerNorm restatement reproduces the reference's layernorm_fwd (rmsnorm.py:655-676)."""
+    g = load_golden(name)
+    out, rstd, mean, _ = oracle.layernorm_fwd(g["x"], g["weight"], g.get("bias"), eps=g["meta"]["eps"])
+    assert _ulp_close(out, g["out"]), name
+    assert _ulp_close(rstd, g["rstd"]), name
+    if "mean" in g:
+        assert _ulp_close(mean, g["mean"]), name
+
+
+@pytest.mark.parametrize("name", LN_CASES)
+def test_package_host_path_reproduces_reference_layernorm(name):
+    g = load_golden(name)
+    kw = {"return_rstd": True, "return_mean": "mean" in g}
+    res = rmsnorm.layernorm_fwd(g["x"], g["weight"], bias=g.get("bias"), eps=g["meta"]["eps"], **kw)
+    assert torch.equal(res[0], g["out"]) and torch.equal(res[1], g["rstd"]), name
+    if "mean" in g:
+        assert torch.equal(res[2], g["mean"]), name
