@@ -186,7 +186,9 @@ const char* rmsnorm_b200_strerror(int status);
  * device-side wait ran out. Synchronises `stream`. */
 int rmsnorm_b200_device_status(void* stream, int32_t* status, int32_t* where, int32_t clear);
 
-/* Upper bound of every device-side wait on the current device (default 2 s). */
+/* Upper bound of every device-side wait on the current device (default 2 s; at least 1 ms,
+ * smaller values return RMSNORM_B200_ERR_INVALID_ARGUMENT). After a failure a kernel still
+ * waits up to max(limit, 2 s) for its in-flight copies before it exits. */
 int rmsnorm_b200_set_wait_timeout_ns(uint64_t timeout_ns);
 
 /* Failure-detection self test: launches one CTA that waits, with the given bound, on an

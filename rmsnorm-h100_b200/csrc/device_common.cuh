@@ -114,13 +114,22 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 
+// Smallest wait limit the host may set, and the floor of the drain after a failure: a CTA
+// never leaves while a bulk copy may still be landing in its shared memory, whatever limit
+// the caller chose for ordinary waits.
+constexpr unsigned long long kMinWaitTimeoutNs = 1000000ull;        // 1 ms
+constexpr unsigned long long kDrainTimeoutFloorNs = 2000000000ull;  // 2 s
+
 // Bounded wait, slow path: returns false (after recording the error) when the phase has
 // not completed within g_wait_timeout_ns, or -- when `honor_abort` -- as soon as another
-// thread of any CTA has recorded an error.
+// thread of any CTA has recorded an error. The drain (honor_abort false) waits at least
+// kDrainTimeoutFloorNs.
 template <bool kClusterScope>
 __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int where, bool honor_abort) {
   const uint64_t t0 = globaltimer_ns();
-  const uint64_t limit = g_wait_timeout_ns;
+  const uint64_t limit = honor_abort ? g_wait_timeout_ns
+                                     : (g_wait_timeout_ns > kDrainTimeoutFloorNs ? g_wait_timeout_ns
+                                                                                  : kDrainTimeoutFloorNs);
   while (true) {
     if (kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) {
       return true;

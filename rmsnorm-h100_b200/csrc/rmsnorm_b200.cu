@@ -971,6 +971,7 @@ extern "C" int rmsnorm_b200_device_status(void* stream, int32_t* status, int32_t
 }
 
 extern "C" int rmsnorm_b200_set_wait_timeout_ns(uint64_t timeout_ns) {
+  if (timeout_ns < kMinWaitTimeoutNs) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
   unsigned long long v = timeout_ns;
   if (cudaMemcpyToSymbol(g_wait_timeout_ns, &v, sizeof(v)) != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
   return RMSNORM_B200_OK;

@@ -77,6 +77,7 @@ def test_invalid_arguments_return_status_codes():
     assert lib.rmsnorm_b200_layernorm_fwd(ctypes.byref(ln), None) == 1
     ln = _lib.LnFwdArgs(rows=0, hidden=16, x=0x1000)
     assert lib.rmsnorm_b200_layernorm_fwd(ctypes.byref(ln), None) == 0
+    assert lib.rmsnorm_b200_set_wait_timeout_ns(10) == 1  # below the 1 ms floor: refused on the host
     b = _lib.BwdArgs(rows=4, hidden=16, heads=1)  # null pointers
     assert lib.rmsnorm_b200_bwd(ctypes.byref(b), None, 0, None) == 1
     n = ctypes.c_size_t(123)

@@ -513,3 +513,28 @@ def test_split_row_pipeline_variants(monkeypatch, k, lag, dtype):
         plan = _bwd_case(9, N, dtype, has_bias=has_bias)
         if "bwd_stream" in plan:
             assert "P=" in plan and f"K={k}" in plan, plan
+
+
+def test_split_row_global_exchange_concurrent_streams(monkeypatch):
+    """Two split-row launches with the global-memory exchange running at the same time on
+    two streams (launch epochs pick different record sets) give the same bits as the same
+    launches one after the other."""
+    monkeypatch.setenv("RMSNORM_B200_XMODE", "1")
+    monkeypatch.setenv("RMSNORM_B200_FORCE_CLUSTER", "4")
+    n = 32768
+    xs = [_g((40, n), BF16, 70 + i) for i in range(2)]
+    w = _g((n,), F32, 72, "weight")
+    seq = [rmsnorm.rmsnorm_fwd(x, w, store_rstd=True) for x in xs]
+    torch.cuda.synchronize()
+    assert "x=global" in _lib.last_plan()
+    streams = [torch.cuda.Stream() for _ in range(2)]
+    outs = [None, None]
+    for rep in range(3):
+        for i, st in enumerate(streams):
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                outs[i] = rmsnorm.rmsnorm_fwd(xs[i], w, store_rstd=True)
+        torch.cuda.synchronize()
+        for i in range(2):
+            assert torch.equal(outs[i][0], seq[i][0]) and torch.equal(outs[i][2], seq[i][2]), (rep, i)
+    assert _lib.device_status(DEV) == (0, 0)
