@@ -54,7 +54,9 @@ def _sharded_worker(rank, world, port, rows, n, heads, result_q):
         out, _, rstd = rd.rmsnorm_fwd_sharded(xs, w, b, store_rstd=True)
         dx, dw, db, _ = rd.rmsnorm_bwd_sharded(xs, w, ys, rstd, has_bias=True, bias=b)
         s, e = rd.row_range(rows, rank, world)
-        result_q.put((rank, s, e, out, dx, dw, db))
+        # numpy arrays travel by value: a tensor would be handed over through a shared-memory
+        # handle that disappears when this process exits before the parent unpickles it
+        result_q.put((rank, s, e) + tuple(t.numpy() for t in (out, dx, dw, db)))
     finally:
         dist.destroy_process_group()
 
@@ -69,6 +71,7 @@ def test_row_sharded_fwd_bwd_equals_single_process(rows, n, heads):
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in range(world)]
+    results = [r[:3] + tuple(torch.from_numpy(a) for a in r[3:]) for r in results]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

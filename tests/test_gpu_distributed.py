@@ -52,7 +52,8 @@ def _worker(rank, world, port, q):
         dx, dw, db, _ = rd.rmsnorm_bwd_sharded(ro, w, ds, rstd, has_bias=True, bias=b)
         torch.cuda.synchronize(dev)
         s, e = rd.row_range(rows, rank, world)
-        q.put((rank, s, e, out.cpu(), dx.cpu(), dw.cpu(), db.cpu()))
+        # numpy arrays travel by value (a tensor's shared-memory handle dies with this process)
+        q.put((rank, s, e) + tuple(t.cpu().float().numpy() for t in (out, dx, dw, db)))
     finally:
         dist.destroy_process_group()
 
@@ -69,6 +70,7 @@ def test_two_gpu_row_sharding_matches_single_process():
     for p in procs:
         p.start()
     results = sorted((q.get(timeout=300) for _ in range(world)), key=lambda r: r[0])
+    results = [r[:3] + tuple(torch.from_numpy(a) for a in r[3:]) for r in results]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
@@ -84,8 +86,8 @@ def test_two_gpu_row_sharding_matches_single_process():
     dx, dw, db, _ = rmsnorm.rmsnorm_bwd(ro, w, dy, rstd, has_bias=True, bias=b)
     _, _, o_db, s_dw, s_db = oracle.bwd(ro.cpu(), w.cpu(), dy.cpu(), rstd.cpu(), has_bias=True)
     for rank, s, e, o, g, gw, gb in results:
-        assert torch.equal(o, out[s:e].cpu())           # the forward is row-local: bitwise equal
-        assert torch.equal(g, dx[s:e].cpu())            # so is dx
+        assert torch.equal(o, out[s:e].cpu().float())   # the forward is row-local: bitwise equal
+        assert torch.equal(g, dx[s:e].cpu().float())    # so is dx
         oracle.check_reduction(gw, dw.cpu(), s_dw, f"rank {rank} dweight")
         oracle.check_reduction(gb, db.cpu(), s_db, f"rank {rank} dbias")
     assert torch.equal(results[0][5], results[1][5]) and torch.equal(results[0][6], results[1][6])
