@@ -204,7 +204,8 @@ void set_prefetch(StreamPlan& pl) {
 // per thread. `force_p` (0 = free) pins the cluster size. Returns false (with a reason)
 // when the shape is outside what the streaming kernels take.
 bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], bool rstd_staged,
-                      int max_vecs, const BlockCfg& bc, int force_p, StreamPlan* out, std::string* why) {
+                      int max_vecs, const BlockCfg& bc, int force_p, StreamPlan* out, std::string* why,
+                      bool one_sweep = false) {
   StreamPlan pl = {};
   if (N64 % 8 != 0 || N64 > (int64_t(1) << 30)) { *why = "hidden % 8 != 0"; return false; }
   const int N = static_cast<int>(N64);
@@ -337,7 +338,7 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
   const int dflt_stage = (pl.seg_mode ? (rstd_staged ? 128 : 64) : 48) * 1024;
   const int target = env_int("RMSNORM_B200_STAGE_BYTES", dflt_stage) * T / kBlockLarge;
   int R = pl.rps;
-  if (P == 1) {
+  if (P == 1 && !one_sweep) {  // one_sweep: one row per row group per tile
     const int64_t m = std::max<int64_t>(1, target / (static_cast<int64_t>(pl.rps) * per_row));
     R = static_cast<int>(pl.rps * m);
     const int64_t rows_needed = (pl.nrows + pl.rps - 1) / pl.rps * pl.rps;
@@ -693,7 +694,8 @@ int do_ln(const rmsnorm_b200_ln_fwd_args* a, cudaStream_t stream) {
     StreamPlan pl;
     const int in_bytes[3] = {elem_bytes(a->x_dtype), 0, 0};
     // rows are never split across CTAs: a row that does not fit one CTA takes the generic path
-    if (make_stream_plan(a->rows, a->hidden, 1, in_bytes, false, kMaxVecs, kLarge, 1, &pl, &why)) {
+    // one row per row group per tile: the LayerNorm row loop pipelines rows tile by tile
+    if (make_stream_plan(a->rows, a->hidden, 1, in_bytes, false, kMaxVecs, kLarge, 1, &pl, &why, true)) {
       FwdParams p = {};
       p.x = a->x; p.w = a->weight; p.b = a->bias; p.out = a->out;
       p.rstd = a->rstd; p.mean = a->mean;

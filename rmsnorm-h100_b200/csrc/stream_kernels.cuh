@@ -37,12 +37,16 @@ namespace rmsb200 {
 constexpr int kXSlots = 8;  // cluster exchange slots (row sequence number mod 8)
 constexpr int kMaxLag = 3;  // deepest exchange lag the slots allow: kXSlots >= 2 * lag + 2
 
+constexpr int kGroupRed = 4;  // split-phase reductions per row group: 2 statistics x 2 rows in flight
+
 struct SmemLayout {
   uint64_t* full;   // [kMaxStages] slot filled
   uint64_t* xbar;   // [kXSlots] cluster exchange barriers
   float* xpart;     // [kXSlots][kMaxCluster] row totals of the cluster's CTAs
   float* red;       // [2][32] per-warp partials (double buffered)
   int* done;        // [kMaxStages] warps finished with the slot's current tile
+  uint64_t* gbar;   // [16 groups][kGroupRed] split-phase row-group reductions (LayerNorm)
+  float* gpart;     // [kGroupRed][16 warps] their per-warp partials
 };
 
 __device__ __forceinline__ SmemLayout carve_smem(unsigned char* smem, const StreamPlan& pl) {
@@ -53,16 +57,21 @@ __device__ __forceinline__ SmemLayout carve_smem(unsigned char* smem, const Stre
   L.xpart = reinterpret_cast<float*>(L.xbar + kXSlots);
   L.red = L.xpart + kXSlots * kMaxCluster;
   L.done = reinterpret_cast<int*>(L.red + 64);
+  L.gbar = reinterpret_cast<uint64_t*>(L.done + kMaxStages);
+  L.gpart = reinterpret_cast<float*>(L.gbar + 16 * kGroupRed);
   return L;
 }
 
-__device__ __forceinline__ void init_barriers(const SmemLayout& L, const StreamPlan& pl) {
+__device__ __forceinline__ void init_barriers(const SmemLayout& L, const StreamPlan& pl, bool group_red = false) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < pl.S; ++s) {
       mbar_init(&L.full[s], 1);
       L.done[s] = 0;
     }
     for (int s = 0; s < kXSlots; ++s) mbar_init(&L.xbar[s], 1);
+    if (group_red)  // one arrival per warp of the row group
+      for (int g = 0; g < pl.rps; ++g)
+        for (int j = 0; j < kGroupRed; ++j) mbar_init(&L.gbar[g * kGroupRed + j], pl.G >> 5);
     fence_mbar_init();
   }
   __syncthreads();
@@ -100,6 +109,27 @@ __device__ __forceinline__ float group_sum(float v, const StreamPlan& pl, const 
     v = warp_sum(lane < nw ? red[lane] : 0.f);
   }
   return v;
+}
+
+// Split-phase row-group reduction (LayerNorm row mode): group_post stores the warp's
+// partial for reduction slot j (statistic x row parity) and arrives on the group's
+// mbarrier without waiting; group_take waits (bounded) for all warps of the group and sums
+// their partials in warp order (same bits in every thread). The slot's k-th use completes
+// phase k: a warp posts use k+1 only after it took use k, which needed every warp's post
+// of use k, so every warp has read use k-1's partials by then.
+__device__ __forceinline__ void group_post(float v, const SmemLayout& L, int gid, int warp, int lane, int j) {
+  v = warp_sum(v);
+  if (lane == 0) {
+    L.gpart[j * 16 + warp] = v;
+    mbar_arrive(&L.gbar[gid * kGroupRed + j]);
+  }
+}
+
+__device__ __forceinline__ float group_take(const StreamPlan& pl, const SmemLayout& L, int gid, int lane, int j,
+                                            uint32_t use) {
+  mbar_wait(&L.gbar[gid * kGroupRed + j], use & 1u, kSiteFwdCluster);
+  const int nw = pl.G >> 5;
+  return warp_sum(lane < nw ? L.gpart[j * 16 + gid * nw + lane] : 0.f);
 }
 
 // Cluster exchange of a row total (rows split over the P CTAs of a cluster, one row group
@@ -278,7 +308,11 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
     }
   }
   const XCtx xc{p.xrec, p.xepoch << 1, cid * pl.P};
-  init_barriers(L, pl);
+  constexpr bool kLNMode = kLN;
+  // LayerNorm row mode: rows pipelined tile by tile (the planner gives one row per group
+  // per tile and at least two slots)
+  const bool ln_rows = kLNMode && !pl.seg_mode && pl.R == pl.rps && pl.S >= 2;
+  init_barriers(L, pl, ln_rows);
 
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const uint64_t pol = l2_policy_evict_first();
@@ -476,7 +510,70 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
     }
   };
 
-  if (active_warp && pl.P == 1) {
+  if (active_warp && ln_rows) {
+    // --------- LayerNorm rows, pipelined one tile deep (tiles hold one row per group) ---------
+    // Iteration q: A(q) = sum of row q, posted; C(q-1) = output of row q-1 once its
+    // variance is in; B(q) = squared deviations of row q once its mean is in, posted.
+    // Every wait is covered by a pass of independent work. Needs S >= 2.
+    int s = 0, sp = 0;
+    uint32_t ph = 0;
+    float mean_p = 0.f;
+    bool act_p = false;
+    int64_t row_p = 0;
+    const X* xs_p = nullptr;
+    for (int64_t q = 0; q <= n_local; ++q) {
+      float mean_q = 0.f;
+      bool act_q = false;
+      int64_t row_q = 0;
+      const X* xs_q = nullptr;
+      const uint32_t par = static_cast<uint32_t>(q) & 1u;
+      if (q < n_local) {
+        mbar_wait(&L.full[s], ph, kSiteFwdFull);
+        const int64_t row0 = (cid + q * ncl) * pl.R;
+        act_q = in_group && row0 + gid < pl.nrows;
+        row_q = row0 + gid;
+        xs_q = stage_x(s) + gid * xs_stride;
+        float part = 0.f;
+        if (act_q) {
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k)
+            if ((vmask >> k) & 1u) part += ln_sum(xs_q + k * G8);
+        }
+        group_post(part, L, gid, warp, lane, 0 + par);
+      }
+      if (q >= 1) {
+        const float var = group_take(pl, L, gid, lane, 2 + (par ^ 1u), static_cast<uint32_t>((q - 1) >> 1)) * inv_n;
+        const float rstd = rsqrtf(var + p.eps);
+        if (act_p) {
+          OT* op = static_cast<OT*>(p.out) + row_p * pl.W + gl * 8;
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k)
+            if ((vmask >> k) & 1u) ln_emit(xs_p + k * G8, op + k * G8, mean_p, rstd, k);
+          if (gl == 0) {
+            if (p.rstd != nullptr) p.rstd[row_p] = rstd;
+            if (p.mean != nullptr) p.mean[row_p] = mean_p;
+          }
+        }
+        if (release_slot(L, sp, nwarps) && q - 1 + S < n_local) issue_unit(q - 1 + S, sp);
+      }
+      if (q < n_local) {
+        mean_q = group_take(pl, L, gid, lane, 0 + par, static_cast<uint32_t>(q >> 1)) * inv_n;
+        float part = 0.f;
+        if (act_q) {
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k)
+            if ((vmask >> k) & 1u) part += ln_dev(xs_q + k * G8, mean_q);
+        }
+        group_post(part, L, gid, warp, lane, 2 + par);
+        sp = s;
+        if (++s == S) { s = 0; ph ^= 1u; }
+      }
+      mean_p = mean_q;
+      act_p = act_q;
+      row_p = row_q;
+      xs_p = xs_q;
+    }
+  } else if (active_warp && pl.P == 1) {
     // ------------------------------- tile loop -------------------------------
     int s = 0;
     uint32_t ph = 0;

@@ -52,7 +52,7 @@ constexpr int kBlockLarge = 512;
 constexpr int kBlockSmall = 256;
 constexpr int kMaxStages = 16;
 constexpr int kMaxCluster = 16;
-constexpr int kSmemReserve = 1280;   // barriers + reduction scratch after the stages
+constexpr int kSmemReserve = 2048;   // barriers + reduction scratch after the stages
 
 // Row-total exchange of split rows (StreamPlan::xmode).
 constexpr int kXCluster = 0;
