@@ -366,6 +366,16 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
   const int ring = env_int("RMSNORM_B200_RING_BYTES", 100 * 1024) * T / kBlockLarge;
   const int s_fit = std::max(1, std::min<int>(max_s, budget / static_cast<int>(stage)));
   pl.S = std::min(s_fit, std::max(2, ring / static_cast<int>(stage)));
+  // Row-mode rows pipelined one tile deep keep two tiles resident, so the ring gets one more
+  // slot. Measured on B200: a gain for forwards whose CTA holds several row groups (cfg 1:
+  // +2 %), a loss where one row fills the CTA (-1 % to -5 %) and for backwards (-6 % at
+  // N = 4096), so by default only the former pipeline (LayerNorm always does).
+  pl.pipe_rows = 0;
+  const int pipe = env_int("RMSNORM_B200_PIPE_ROWS", -1);  // -1 auto, 0 off, 1 on
+  if (!pl.seg_mode && R == pl.rps && (pipe == 1 || (pipe < 0 && pl.rps >= 2 && !rstd_staged))) {
+    pl.pipe_rows = 1;
+    pl.S = std::min(s_fit, pl.S + 1);
+  }
   pl.ntiles = (pl.nrows + R - 1) / R;
   set_prefetch(pl);
   *out = pl;

@@ -111,12 +111,14 @@ __device__ __forceinline__ float group_sum(float v, const StreamPlan& pl, const 
   return v;
 }
 
-// Split-phase row-group reduction (LayerNorm row mode): group_post stores the warp's
-// partial for reduction slot j (statistic x row parity) and arrives on the group's
-// mbarrier without waiting; group_take waits (bounded) for all warps of the group and sums
-// their partials in warp order (same bits in every thread). The slot's k-th use completes
-// phase k: a warp posts use k+1 only after it took use k, which needed every warp's post
-// of use k, so every warp has read use k-1's partials by then.
+// Split-phase row-group reduction (pipelined rows): group_post stores the warp's partial
+// for reduction slot j and arrives on the group's mbarrier without waiting; group_take
+// waits (bounded) for all warps of the group and sums their partials in warp order (same
+// bits in every thread). The slot's k-th use completes phase k. Slots are reused only
+// after every warp has read them: LayerNorm uses slots {mean, variance} x row parity (its
+// two reductions per row order the warps); the one-reduction loops, where a warp posts row
+// q before it takes row q-1, use row mod 4 (a warp posts row q+4 after taking row q+2,
+// which needed every warp's post of row q+2, made after its take of row q).
 __device__ __forceinline__ void group_post(float v, const SmemLayout& L, int gid, int warp, int lane, int j) {
   v = warp_sum(v);
   if (lane == 0) {
@@ -312,7 +314,9 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
   // LayerNorm row mode: rows pipelined tile by tile (the planner gives one row per group
   // per tile and at least two slots)
   const bool ln_rows = kLNMode && !pl.seg_mode && pl.R == pl.rps && pl.S >= 2;
-  init_barriers(L, pl, ln_rows);
+  // RMSNorm row mode pipelined the same way (one reduction) when the planner asked for it
+  const bool rms_rows = !kLNMode && pl.pipe_rows && !pl.seg_mode && pl.P == 1 && pl.R == pl.rps && pl.S >= 3;
+  init_barriers(L, pl, ln_rows || rms_rows);
 
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const uint64_t pol = l2_policy_evict_first();
@@ -573,6 +577,58 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       row_p = row_q;
       xs_p = xs_q;
     }
+  } else if (active_warp && rms_rows) {
+    // --------- RMSNorm rows, pipelined one tile deep ---------
+    // Iteration q: sum of squares of row q, posted; output of row q-1 once its sum is in.
+    int s = 0, sp = 0;
+    uint32_t ph = 0;
+    bool act_p = false;
+    int64_t row_p = 0;
+    const X* xs_p = nullptr;
+    const RTe* rs_p = nullptr;
+    for (int64_t q = 0; q <= n_local; ++q) {
+      bool act_q = false;
+      int64_t row_q = 0;
+      const X* xs_q = nullptr;
+      const RTe* rs_q = nullptr;
+      const uint32_t slot = static_cast<uint32_t>(q) & 3u;
+      if (q < n_local) {
+        mbar_wait(&L.full[s], ph, kSiteFwdFull);
+        const int64_t row0 = (cid + q * ncl) * pl.R;
+        act_q = in_group && row0 + gid < pl.nrows;
+        row_q = row0 + gid;
+        xs_q = stage_x(s) + gid * xs_stride;
+        rs_q = stage_r(s) + gid * xs_stride;
+        float part[kVecs];
+        float ss = 0.f;
+        if (act_q) {
+          pass1(xs_q, rs_q, part);
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) ss += part[k];
+        }
+        group_post(ss, L, gid, warp, lane, slot);
+      }
+      if (q >= 1) {
+        const float tot = group_take(pl, L, gid, lane, (slot + 3u) & 3u, static_cast<uint32_t>((q - 1) >> 2));
+        const float r = rsqrtf(fmaf(tot, inv_n, p.eps));
+        if (act_p) {
+          float rstd_k[kVecs];
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) rstd_k[k] = r;
+          pass2(xs_p, rs_p, row_p, rstd_k);
+          if (p.rstd != nullptr && gl == 0) p.rstd[row_p] = r;
+        }
+        if (release_slot(L, sp, nwarps) && q - 1 + S < n_local) issue_unit(q - 1 + S, sp);
+      }
+      if (q < n_local) {
+        sp = s;
+        if (++s == S) { s = 0; ph ^= 1u; }
+      }
+      act_p = act_q;
+      row_p = row_q;
+      xs_p = xs_q;
+      rs_p = rs_q;
+    }
   } else if (active_warp && pl.P == 1) {
     // ------------------------------- tile loop -------------------------------
     int s = 0;
@@ -802,7 +858,9 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     }
   }
   const XCtx xc{p.xrec, p.xepoch << 1, cid * pl.P};
-  init_barriers(L, pl);
+  // row mode with one row per group per tile: rows pipelined one tile deep (when planned)
+  const bool rows_pipe = pl.pipe_rows && !pl.seg_mode && pl.P == 1 && pl.R == pl.rps && pl.S >= 3;
+  init_barriers(L, pl, rows_pipe);
 
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const int rstd_per_row = pl.seg_mode ? pl.heads : 1;
@@ -966,7 +1024,55 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     }
   };
 
-  if (active_warp && pl.P == 1) {
+  if (active_warp && rows_pipe) {
+    // --------- rows pipelined one tile deep ---------
+    // Iteration q: dot products (and dweight / dbias) of row q, posted; dx of row q-1
+    // once its dot product is in.
+    int s = 0, sp = 0;
+    uint32_t ph = 0;
+    bool act_p = false;
+    int64_t row_p = 0;
+    float rstd_p = 0.f;
+    for (int64_t q = 0; q <= n_local; ++q) {
+      bool act_q = false;
+      int64_t row_q = 0;
+      float rstd_q = 0.f;
+      const uint32_t slot = static_cast<uint32_t>(q) & 3u;
+      if (q < n_local) {
+        mbar_wait(&L.full[s], ph, kSiteBwdFull);
+        const int64_t row0 = (cid + q * ncl) * pl.R;
+        act_q = in_group && row0 + gid < pl.nrows;
+        row_q = row0 + gid;
+        float dot = 0.f;
+        if (act_q) {
+          const RowPtrs rp = row_ptrs(s, gid);
+          float part[kVecs], rstd_k[kVecs];
+          pass1(rp, part, rstd_k);
+          rstd_q = rp.rstd[0];
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) dot += part[k];
+        }
+        group_post(dot, L, gid, warp, lane, slot);
+      }
+      if (q >= 1) {
+        const float c = group_take(pl, L, gid, lane, (slot + 3u) & 3u, static_cast<uint32_t>((q - 1) >> 2)) * inv_n;
+        if (act_p) {
+          float rstd_k[kVecs], c_k[kVecs];
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) { rstd_k[k] = rstd_p; c_k[k] = c; }
+          pass2(row_ptrs(sp, gid), row_p, rstd_k, c_k);
+        }
+        if (release_slot(L, sp, nwarps) && q - 1 + S < n_local) issue_unit(q - 1 + S, sp);
+      }
+      if (q < n_local) {
+        sp = s;
+        if (++s == S) { s = 0; ph ^= 1u; }
+      }
+      act_p = act_q;
+      row_p = row_q;
+      rstd_p = rstd_q;
+    }
+  } else if (active_warp && pl.P == 1) {
     // ------------------------------- tile loop -------------------------------
     int s = 0;
     uint32_t ph = 0;

@@ -35,6 +35,7 @@ struct StreamPlan {
   int32_t kpc_shift;  // log2(thread vectors per chunk) = log2(kVecs / K)
   int32_t xmode;      // P > 1: kXCluster (DSMEM exchange) or kXGlobal (global-memory records)
   int32_t pf;         // ring units between a refill and the L2 prefetch issued with it (0 = none)
+  int32_t pipe_rows;  // RMSNorm row mode: rows pipelined one tile deep (ring holds one more slot)
   int32_t lag;        // rows the cluster exchange lags pass 1 by (P > 1): pass 2 of row i-lag
                       // follows pass 1 of row i
   int64_t nrows;      // super-rows

@@ -538,3 +538,28 @@ def test_split_row_global_exchange_concurrent_streams(monkeypatch):
         for i in range(2):
             assert torch.equal(outs[i][0], seq[i][0]) and torch.equal(outs[i][2], seq[i][2]), (rep, i)
     assert _lib.device_status(DEV) == (0, 0)
+
+
+@pytest.mark.parametrize("pipe", ["0", "1"])
+@pytest.mark.parametrize("rows,n", [(8192, 4096), (4096, 8192), (2048, 16384)])
+def test_row_pipelining_on_and_off(monkeypatch, pipe, rows, n):
+    """Row-mode rows with and without the one-tile-deep pipeline (split-phase row-group
+    reductions), at sizes with many tiles per CTA so warps drift apart: forward with and
+    without residual (rstd checked row by row) and backward."""
+    from gpu_ref import bwd_check, fwd_max_err
+    monkeypatch.setenv("RMSNORM_B200_PIPE_ROWS", pipe)
+    x = _gpu_gen((rows, n), BF16, 80 + n)
+    r = _gpu_gen((rows, n), BF16, 81 + n)
+    w = _gpu_gen((n,), F32, 82, "weight")
+    b = _gpu_gen((n,), F32, 83, "bias")
+    out, _, rstd = rmsnorm.rmsnorm_fwd(x, w, store_rstd=True)
+    plan = _lib.last_plan()
+    assert "mode=row" in plan, plan
+    assert fwd_max_err(x, w, None, None, out, None, rstd, 1e-6, 1.6e-2) <= 1.0, plan
+    out, ro, rstd = rmsnorm.rmsnorm_fwd(x, w, b, r, residual_dtype=F32, store_rstd=True)
+    assert fwd_max_err(x, w, b, r, out, ro, rstd, 1e-6, 1.6e-2) <= 1.0, _lib.last_plan()
+    dy = _gpu_gen((rows, n), BF16, 84 + n)
+    dx, dw, _, _ = rmsnorm.rmsnorm_bwd(x, w, dy, rstd)
+    dx_err, dw_err = bwd_check(x, w, dy, rstd, dx, dw, 1.6e-2, chunk=512)
+    assert dx_err <= 1.0 and dw_err <= 1.0, (dx_err, dw_err, _lib.last_plan())
+    assert _lib.device_status(DEV) == (0, 0)
