@@ -221,6 +221,51 @@ __device__ __forceinline__ float seg_sum(float v, int width, unsigned mask) {
   return v;
 }
 
+// Sums each of a thread's kV values over its aligned segment of `vs` lanes (the lanes own
+// the same position in kV different segments) and applies `post` to each sum. For kV = 4
+// or 2 and vs >= kV the reduction is transposed: the first butterfly levels split the
+// values between lane halves, so log2(vs) shuffles finish all kV sums, each lane applies
+// `post` to the one sum it holds, and kV shuffles hand every lane all kV results (instead
+// of kV * log2(vs) shuffles and kV posts). Lanes holding the same sum combined the same
+// partials by commutative additions, so every lane of a segment gets the same bits.
+template <int kV, typename Post>
+__device__ __forceinline__ void seg_reduce(const float (&v)[kV], float (&out)[kV], int vs, unsigned mask, Post post) {
+  const int lane = threadIdx.x & 31;
+  if constexpr (kV == 4 || kV == 2) {
+    if (vs >= kV) {
+      const int h1 = vs >> 1;
+      const bool b1 = (lane & h1) != 0;
+      float a;
+      int done;  // butterfly levels left to run with plain exchanges
+      if constexpr (kV == 4) {
+        const int h2 = vs >> 2;
+        const bool b2 = (lane & h2) != 0;
+        // level 1: keep values {0,1} (b1 = 0) or {2,3} (b1 = 1) and send the other pair
+        const float p0 = (b1 ? v[2] : v[0]) + __shfl_xor_sync(mask, b1 ? v[0] : v[2], h1);
+        const float p1 = (b1 ? v[3] : v[1]) + __shfl_xor_sync(mask, b1 ? v[1] : v[3], h1);
+        // level 2: keep one of the two; this lane now sums value 2*b1 + b2
+        a = (b2 ? p1 : p0) + __shfl_xor_sync(mask, b2 ? p0 : p1, h2);
+        done = h2 >> 1;
+      } else {
+        a = (b1 ? v[1] : v[0]) + __shfl_xor_sync(mask, b1 ? v[0] : v[1], h1);
+        done = h1 >> 1;
+      }
+      for (int off = done; off > 0; off >>= 1) a += __shfl_xor_sync(mask, a, off);
+      const float mine = post(a);
+      const int base = lane & ~(vs - 1);
+      const int low = lane & ((kV == 4 ? (vs >> 2) : (vs >> 1)) - 1);
+#pragma unroll
+      for (int k = 0; k < kV; ++k) {
+        const int sel = kV == 4 ? (((k >> 1) ? (vs >> 1) : 0) | ((k & 1) ? (vs >> 2) : 0)) : (k ? (vs >> 1) : 0);
+        out[k] = __shfl_sync(mask, mine, base | sel | low);
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kV; ++k) out[k] = post(seg_sum(v[k], vs, mask));
+}
+
 // After a failure: let every copy still in flight land before the CTA exits (waits bounded
 // by time only). The ring held n_units loads (tiles, or row-slice chunks); slot s last held
 // unit u_last(s).
@@ -655,8 +700,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
         // segment (seg mode) or row-group (row mode) sum of part[], scaled by `scale`
         auto reduce_k = [&](const float (&pt)[kVecs], float (&res)[kVecs], float scale) {
           if (pl.seg_mode) {
-#pragma unroll
-            for (int k = 0; k < kVecs; ++k) res[k] = seg_sum(pt[k], pl.vs, amask) * scale;
+            seg_reduce<kVecs>(pt, res, pl.vs, amask, [&](float t) { return t * scale; });
           } else {
             float t = 0.f;
 #pragma unroll
@@ -684,9 +728,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
         } else {
           pass1(xs, rs, part);
           if (pl.seg_mode) {
-#pragma unroll
-            for (int k = 0; k < kVecs; ++k)
-              rstd_k[k] = rsqrtf(fmaf(seg_sum(part[k], pl.vs, amask), inv_n, p.eps));
+            seg_reduce<kVecs>(part, rstd_k, pl.vs, amask, [&](float t) { return rsqrtf(fmaf(t, inv_n, p.eps)); });
           } else {
             float ss = 0.f;
 #pragma unroll
@@ -1091,8 +1133,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
         float part[kVecs], rstd_k[kVecs], c_k[kVecs];
         pass1(rp, part, rstd_k);
         if (pl.seg_mode) {
-#pragma unroll
-          for (int k = 0; k < kVecs; ++k) c_k[k] = seg_sum(part[k], pl.vs, amask) * inv_n;
+          seg_reduce<kVecs>(part, c_k, pl.vs, amask, [&](float t) { return t * inv_n; });
         } else {
           float dot = 0.f;
 #pragma unroll
