@@ -1,25 +1,33 @@
-// stream_kernels.cuh -- the persistent, TMA-staged forward and backward kernels.
+// stream_kernels.cuh -- the persistent, TMA-staged forward (RMSNorm and LayerNorm) and
+// backward kernels.
 //
-// Structure (both directions):
-//   * one CTA of 512 threads per SM (or 256 threads, two per SM), persistent over tiles
-//     assigned round-robin (local tile q of cluster c is tile c + q * clusters);
+// Structure:
+//   * one CTA of 512 threads per SM (or 256 threads, two per SM, for some backwards),
+//     persistent over tiles assigned round-robin (local tile q of CTA group c is tile
+//     c + q * groups);
 //   * tiles stream HBM -> shared memory with cp.async.bulk (TMA bulk copies, no tensor map,
 //     no multicast; one copy per tensor per tile) into an S-slot ring; each slot's "full"
 //     mbarrier counts the landing bytes. There is no CTA-wide barrier per tile: every warp
 //     waits on the slot's mbarrier, and when it is done with the slot it bumps the slot's
 //     shared-memory counter; the last warp to finish refills the slot with tile q + S;
-//   * threads read 8-element vectors from shared memory, reduce the row (xor shuffles in a
-//     warp; one named barrier + one shared load + a second shuffle tree across the warps of
-//     a row group; for rows split over a cluster of P CTAs, warp 0 sends the CTA's total to
-//     every peer in parallel with st.async (lane q -> peer q) and every warp sums the P
-//     totals it receives), then re-read the slot and write outputs with 16-byte coalesced
-//     streaming stores. Split rows are software-pipelined one row deep: pass 1 of row i and
-//     its exchange overlap pass 2 of row i-1;
-//   * every per-element dtype is a template parameter (absent tensors are `NoT`), so the
-//     inner loops carry no runtime type dispatch;
+//   * threads read 8-element vectors from shared memory and reduce each row:
+//       - per-head rows of up to 32 vectors ("seg" mode): xor shuffles inside a lane
+//         segment, transposed so a thread's values for several heads share the levels;
+//       - whole rows ("row" mode): warp shuffles and one named barrier per row group, or,
+//         for pipelined rows, split-phase reductions through per-group mbarriers so the
+//         output pass of the previous row hides the wait (LayerNorm always, RMSNorm
+//         forwards with several row groups per CTA);
+//       - rows split over P CTAs: warp 0 sends the CTA's total to the peers (st.async into
+//         the cluster's shared memory, or tagged 64-bit records in global memory for
+//         groups of a cooperative grid) and every warp sums the P totals; pass 1 of row i
+//         and its exchange overlap pass 2 of row i - lag;
+//     then they re-read the slot and write outputs with 16-byte streaming stores;
+//   * every per-element dtype, the bias and the LayerNorm mode are template parameters
+//     (absent tensors are `NoT`), so the inner loops carry no runtime type dispatch; the
+//     arithmetic uses sm_100's paired fp32 instructions where that measured faster;
 //   * affine parameters live in registers for the whole kernel (each thread always owns
 //     the same columns), so dweight/dbias accumulate in registers and are written once
-//     per (cluster, row group) as a partial row; a second kernel sums the partials in a
+//     per (CTA group, row group) as a partial row; a second kernel sums the partials in a
 //     fixed order.
 // Every wait is bounded. A wait that gives up records an error in the device status word;
 // from then on every wait of every CTA returns at once, so the kernel runs to its end on
