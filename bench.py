@@ -272,8 +272,9 @@ def traffic_for(workload):
 # CPU baseline: the reference's PyTorch CPU path (oracle port) on a bounded row sample
 # ----------------------------------------------------------------------------------------
 def cpu_sample_rows(w):
-    # about 16M elements per step: long enough to time, short enough to repeat
-    return max(1, min(w["rows"], (16 << 20) // w["n"]))
+    # up to 32M elements per step: the whole of cfg 1 (8192 x 4096), a row sample of the
+    # larger configs (2048 rows of cfg 2) -- long enough to time, short enough to repeat
+    return max(1, min(w["rows"], (32 << 20) // w["n"]))
 
 
 def cpu_step_fn(w, rows):
