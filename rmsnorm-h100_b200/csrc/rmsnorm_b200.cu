@@ -512,6 +512,27 @@ constexpr int kBwdVecsDb = 2;
 int bwd_max_vecs(bool has_db) { return has_db ? kBwdVecsDb : kMaxVecs; }
 
 // (x, dout, dx, dresidual_out, dresidual), dbias, launch shape
+// Per-head backward (x, dy and dx of one dtype, no residual gradients): kernels that stage
+// each tile's rstd block with one bulk copy.
+BwdKernel pick_bwd_per_head(int x, int dy, int dx, bool db, bool small) {
+  if (x != dy || x != dx) return nullptr;
+#define RMSB_BWD_PH(XT, XC, BLK, MINB)                                                                  \
+  if (x == XC)                                                                                        \
+    return db ? bwd_stream_kernel<XT, XT, XT, NoT, NoT, true, kBwdVecsDb, BLK, MINB, true>            \
+              : bwd_stream_kernel<XT, XT, XT, NoT, NoT, false, kMaxVecs, BLK, MINB, true>;
+  if (small) {
+    RMSB_BWD_PH(b16, B, kBlockSmall, 2)
+    RMSB_BWD_PH(h16, H, kBlockSmall, 2)
+    RMSB_BWD_PH(float, F, kBlockSmall, 2)
+    return nullptr;
+  }
+  RMSB_BWD_PH(b16, B, kBlockLarge, 1)
+  RMSB_BWD_PH(h16, H, kBlockLarge, 1)
+  RMSB_BWD_PH(float, F, kBlockLarge, 1)
+#undef RMSB_BWD_PH
+  return nullptr;
+}
+
 BwdKernel pick_bwd(int x, int dy, int dx, int dro, int dres, bool db, bool small) {
 #define RMSB_BWD_SHAPE(XT, XC, DT, DC, DXT, DXC, AT, AC, ST, SC, BLK, MINB)                       \
   if (x == XC && dy == DC && dx == DXC && dro == AC && dres == SC)                                 \
@@ -788,6 +809,12 @@ int plan_bwd(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdPlan* bp) {
     const int dres = a->dresidual ? a->dresidual_dtype : NA;
     BwdKernel large = pick_bwd(a->x_dtype, a->dout_dtype, a->dx_dtype, dro, dres, bp->need_db, false);
     BwdKernel small = pick_bwd(a->x_dtype, a->dout_dtype, a->dx_dtype, dro, dres, bp->need_db, true);
+    if (a->heads > 1 && dro == NA && dres == NA) {  // per-head rows: bulk rstd staging
+      BwdKernel ph_large = pick_bwd_per_head(a->x_dtype, a->dout_dtype, a->dx_dtype, bp->need_db, false);
+      BwdKernel ph_small = pick_bwd_per_head(a->x_dtype, a->dout_dtype, a->dx_dtype, bp->need_db, true);
+      if (ph_large) large = ph_large;
+      if (ph_small) small = ph_small;
+    }
     const int force_p = env_int("RMSNORM_B200_FORCE_CLUSTER", 0);
     const int shape = env_int("RMSNORM_B200_BWD_SHAPE", 0);  // 0 auto, 1 large only, 2 small only
     if (!large && !small) why = "dtype combination";

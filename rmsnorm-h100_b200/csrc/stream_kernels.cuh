@@ -840,8 +840,9 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
 // Backward: dx in one pass from the saved rstd; dweight / dbias per-CTA partial rows.
 // =======================================================================================
 // Tile `tile` (or chunk j of this CTA's slice of row `tile`) into slot s; every chunk of a
-// split row carries the row's rstd.
-template <typename X, typename DY, typename DROT>
+// split row carries the row's rstd. kRstdBulk (per-head kernels): the tile's rstd block
+// (rows x heads floats) comes with one bulk copy when it is 16-byte aligned and sized.
+template <typename X, typename DY, typename DROT, bool kRstdBulk>
 __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& pl, const SmemLayout& L,
                                           unsigned char* smem, int64_t tile, int j, int s, int64_t slice_elt0,
                                           int rstd_per_row, uint64_t pol, int64_t pf_tile = -1, int pf_j = 0) {
@@ -849,19 +850,26 @@ __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& 
   const int64_t row0 = tile * pl.R;
   const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
   fence_proxy_async_smem();
-  // rstd of the tile's rows: plain async copies, tracked by the same mbarrier
+  // rstd of the tile's rows, tracked by the same mbarrier: one bulk copy when the block
+  // is 16-byte aligned and sized (per-head tiles: rows x heads floats), else plain async
+  // copies (a row-mode tile needs only a few floats)
   float* rdst = reinterpret_cast<float*>(st + pl.off[3]);
   const float* rsrc = p.rstd + row0 * rstd_per_row;
   const int cnt = rows * rstd_per_row;
-  int c = 0;
-  if ((reinterpret_cast<uintptr_t>(rsrc) & 15u) == 0)
-    for (; c + 4 <= cnt; c += 4) cp_async_16(rdst + c, rsrc + c);
-  for (; c < cnt; ++c) cp_async_4(rdst + c, rsrc + c);
-  cp_async_arrive(&L.full[s]);
+  const uint32_t rbytes = static_cast<uint32_t>(cnt) * 4u;
+  const bool rbulk = kRstdBulk && (reinterpret_cast<uintptr_t>(rsrc) & 15u) == 0 && (rbytes & 15u) == 0;
+  if (!rbulk) {
+    int c = 0;
+    if ((reinterpret_cast<uintptr_t>(rsrc) & 15u) == 0)
+      for (; c + 4 <= cnt; c += 4) cp_async_16(rdst + c, rsrc + c);
+    for (; c < cnt; ++c) cp_async_4(rdst + c, rsrc + c);
+    cp_async_arrive(&L.full[s]);
+  }
   const uint32_t b0 = static_cast<uint32_t>(rows) * pl.row_bytes[0];
   const uint32_t b1 = static_cast<uint32_t>(rows) * pl.row_bytes[1];
   const uint32_t b2 = Present<DROT>::value ? static_cast<uint32_t>(rows) * pl.row_bytes[2] : 0u;
-  mbar_arrive_expect_tx(&L.full[s], b0 + b1 + b2);
+  mbar_arrive_expect_tx(&L.full[s], b0 + b1 + b2 + (rbulk ? rbytes : 0u));
+  if (rbulk) bulk_load(rdst, rsrc, rbytes, &L.full[s], pol);
   const int64_t e0 = row0 * pl.W + slice_elt0 + static_cast<int64_t>(j) * (pl.row_bytes[0] / sizeof(X));
   bulk_load(st + pl.off[0], static_cast<const X*>(p.x) + e0, b0, &L.full[s], pol);
   bulk_load(st + pl.off[1], static_cast<const DY*>(p.dy) + e0, b1, &L.full[s], pol);
@@ -879,9 +887,9 @@ __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& 
 }
 
 // X: saved input dtype; DY: dout dtype; DXT: dx dtype; DROT: dresidual_out dtype (NoT =
-// none); DREST: dresidual dtype (NoT = not written).
+// none); DREST: dresidual dtype (NoT = not written); kRstdBulk: see bwd_issue.
 template <typename X, typename DY, typename DXT, typename DROT, typename DREST, bool kHasDb, int kVecs,
-          int kBlock, int kMinBlocks>
+          int kBlock, int kMinBlocks, bool kRstdBulk = false>
 __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const BwdParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr bool kDro = Present<DROT>::value;
@@ -924,7 +932,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   auto issue_unit = [&](int64_t u, int s) {
     const int64_t v = u + pl.pf;
     const bool pf = pl.pf > 0 && v < n_units;
-    bwd_issue<X, DY, DROT>(p, pl, L, smem, cid + (u >> kshift) * ncl, static_cast<int>(u & (K - 1)), s, slice_elt0,
+    bwd_issue<X, DY, DROT, kRstdBulk>(p, pl, L, smem, cid + (u >> kshift) * ncl, static_cast<int>(u & (K - 1)), s, slice_elt0,
                            rstd_per_row, pol, pf ? cid + (v >> kshift) * ncl : -1, static_cast<int>(v & (K - 1)));
   };
   if (tid == 0)
