@@ -205,7 +205,7 @@ void set_prefetch(StreamPlan& pl) {
 // when the shape is outside what the streaming kernels take.
 bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], bool rstd_staged,
                       int max_vecs, const BlockCfg& bc, int force_p, StreamPlan* out, std::string* why,
-                      bool one_sweep = false) {
+                      bool one_sweep = false, bool col_mode = false) {
   StreamPlan pl = {};
   if (N64 % 8 != 0 || N64 > (int64_t(1) << 30)) { *why = "hidden % 8 != 0"; return false; }
   const int N = static_cast<int>(N64);
@@ -220,16 +220,26 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
   pl.W = W;
   pl.nrows = rows / H;
   int P = 1;
+  pl.cols = max_vecs;
   if (H > 1) {
     const int vs = N / 8;
     if (!is_pow2(vs) || vs > 32) { *why = "per-head segment not a power of two <= 32 vectors"; return false; }
-    const int per_thread_min = (vrow + max_vecs - 1) / max_vecs;
+    // column mode (col_mode): the fewest columns per thread whose group fits the CTA, each
+    // thread then covering max_vecs / cols super-rows of a sweep
+    int cols = max_vecs;
+    if (col_mode)
+      for (int c = 1; c < max_vecs; c <<= 1) {
+        const int per = (vrow + c - 1) / c;
+        if (vs * ((per + vs - 1) / vs) <= T) { cols = c; break; }
+      }
+    const int per_thread_min = (vrow + cols - 1) / cols;
     const int G = vs * ((per_thread_min + vs - 1) / vs);
     if (G > T) { *why = "per-head super-row too wide"; return false; }
     pl.seg_mode = 1;
     pl.vs = vs;
     pl.G = G;
     pl.vslice = vrow;
+    pl.cols = cols;
   } else if (vrow <= 32) {
     pl.seg_mode = 1;
     pl.vs = pow2_ceil(vrow);
@@ -337,12 +347,13 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
   // bigger tiles.
   const int dflt_stage = (pl.seg_mode ? (rstd_staged ? 128 : 64) : 48) * 1024;
   const int target = env_int("RMSNORM_B200_STAGE_BYTES", dflt_stage) * T / kBlockLarge;
-  int R = pl.rps;
+  const int rstep = pl.rps * (max_vecs / pl.cols);  // super-rows per sweep
+  int R = rstep;
   if (P == 1 && !one_sweep) {  // one_sweep: one row per row group per tile
-    const int64_t m = std::max<int64_t>(1, target / (static_cast<int64_t>(pl.rps) * per_row));
-    R = static_cast<int>(pl.rps * m);
-    const int64_t rows_needed = (pl.nrows + pl.rps - 1) / pl.rps * pl.rps;
-    if (R > rows_needed) R = static_cast<int>(std::max<int64_t>(pl.rps, rows_needed));
+    const int64_t m = std::max<int64_t>(1, target / (static_cast<int64_t>(rstep) * per_row));
+    R = static_cast<int>(rstep * m);
+    const int64_t rows_needed = (pl.nrows + rstep - 1) / rstep * rstep;
+    if (R > rows_needed) R = static_cast<int>(std::max<int64_t>(rstep, rows_needed));
   }
   auto layout = [&](int r) {
     uint32_t off = 0;
@@ -355,8 +366,8 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
     return off;
   };
   uint32_t stage = layout(R);
-  while (2 * stage > static_cast<uint32_t>(budget) && R > pl.rps) {  // keep two stages
-    R -= pl.rps;
+  while (2 * stage > static_cast<uint32_t>(budget) && R > rstep) {  // keep two stages
+    R -= rstep;
     stage = layout(R);
   }
   if (stage > static_cast<uint32_t>(budget)) { *why = "stage does not fit shared memory"; return false; }
@@ -389,11 +400,12 @@ std::string describe(const char* kind, const StreamPlan& pl, int grid) {
   char buf[512];
   std::snprintf(buf, sizeof(buf),
                 "%s mode=%s P=%d x=%s grid=%d clusters=%d T=%d G=%d rps=%d R=%d S=%d stage=%u "
-                "vslice=%d vs=%d K=%d lag=%d pf=%d tiles=%lld",
+                "vslice=%d vs=%d cols=%d K=%d lag=%d pf=%d tiles=%lld",
                 kind, pl.seg_mode ? "seg" : "row", pl.P,
                 pl.P == 1 ? "none" : (pl.xmode == kXGlobal ? "global" : "cluster"), grid, pl.nclusters, pl.T, pl.G,
                 pl.rps,
-                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, pl.K, pl.lag, pl.pf, static_cast<long long>(pl.ntiles));
+                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, pl.cols, pl.K, pl.lag, pl.pf,
+                static_cast<long long>(pl.ntiles));
   return buf;
 }
 
@@ -489,6 +501,24 @@ FwdKernel pick_fwd(int x, int r, int o, int ro, bool bias) {
   RMSB_FWD(b16, B, NoT, NA, float, F, NoT, NA)
   RMSB_FWD(h16, H, NoT, NA, float, F, NoT, NA)
 #undef RMSB_FWD
+  return nullptr;
+}
+
+// Per-head column mode (x and out of one dtype, no residual): `cols` columns and
+// kMaxVecs / cols super-rows per thread per sweep.
+FwdKernel pick_fwd_cols(int x, int o, bool bias, int cols) {
+  if (x != o) return nullptr;
+#define RMSB_FWD_COLS(XT, XC, C)                                                                  \
+  if (x == XC && cols == C)                                                                       \
+    return bias ? fwd_stream_kernel<XT, NoT, XT, NoT, true, false, kMaxVecs, kBlockLarge, 1, C>    \
+                : fwd_stream_kernel<XT, NoT, XT, NoT, false, false, kMaxVecs, kBlockLarge, 1, C>;
+  RMSB_FWD_COLS(b16, B, 1)
+  RMSB_FWD_COLS(h16, H, 1)
+  RMSB_FWD_COLS(float, F, 1)
+  RMSB_FWD_COLS(b16, B, 2)
+  RMSB_FWD_COLS(h16, H, 2)
+  RMSB_FWD_COLS(float, F, 2)
+#undef RMSB_FWD_COLS
   return nullptr;
 }
 
@@ -665,8 +695,23 @@ int do_fwd(const rmsnorm_b200_fwd_args* a, cudaStream_t stream) {
   if (kernel) {
     StreamPlan pl;
     const int in_bytes[3] = {elem_bytes(a->x_dtype), a->residual ? elem_bytes(a->residual_dtype) : 0, 0};
-    if (make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, false, kMaxVecs, kLarge,
-                         env_int("RMSNORM_B200_FORCE_CLUSTER", 0), &pl, &why)) {
+    bool planned = false;
+    // Per-head rows without a residual: column mode, where its kernel exists. Measured on
+    // B200 at (16384, 32, 128) fp16 with per-head weight and bias: the four-column kernel
+    // holds 64 registers of weight / bias and issues about a third more instructions.
+    if (a->heads > 1 && !a->residual && !a->residual_out && env_int("RMSNORM_B200_COL_MODE", 1) &&
+        make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, false, kMaxVecs, kLarge, 0, &pl, &why, false,
+                         true) &&
+        pl.cols < kMaxVecs) {
+      if (FwdKernel kc = pick_fwd_cols(a->x_dtype, a->out_dtype, a->bias != nullptr, pl.cols)) {
+        kernel = kc;
+        planned = true;
+      }
+    }
+    if (!planned)
+      planned = make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, false, kMaxVecs, kLarge,
+                                 env_int("RMSNORM_B200_FORCE_CLUSTER", 0), &pl, &why);
+    if (planned) {
       FwdParams p = {};
       p.x = a->x; p.res = a->residual; p.w = a->weight; p.b = a->bias;
       p.out = a->out; p.ro = a->residual_out; p.rstd = a->rstd;

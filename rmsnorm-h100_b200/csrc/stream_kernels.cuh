@@ -336,8 +336,11 @@ __device__ __forceinline__ void fwd_issue(const FwdParams& p, const StreamPlan& 
 // LayerNorm instead of RMSNorm (no residual; mean, then the mean of squared deviations
 // from the staged tile, out = (x - mean) * rstd * w + b; rows are never split).
 template <typename X, typename RT, typename OT, typename ROT, bool kBias, bool kLN, int kVecs, int kBlock,
-          int kMinBlocks>
+          int kMinBlocks, int kCols = kVecs>
 __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const FwdParams p) {
+  // kCols < kVecs: per-head column mode (thread vector k = column k % kCols of super-row
+  // k / kCols of the thread's group in the sweep); only the tile loop runs in that mode
+  static_assert(kVecs % kCols == 0 && (kCols == kVecs || !kLN), "column mode: RMSNorm tiles only");
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr bool kRes = Present<RT>::value;
   constexpr bool kRO = Present<ROT>::value;
@@ -399,13 +402,13 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
   unsigned vmask = 0;
 #pragma unroll
   for (int k = 0; k < kVecs; ++k)
-    if (in_group && gl + k * G < pl.vslice) vmask |= 1u << k;
+    if (in_group && gl + (k % kCols) * G < pl.vslice) vmask |= 1u << k;
 
   // weight / bias of the thread's columns, as float pairs (element 2i in .x, 2i+1 in .y)
-  float2 wr[kVecs][4];
-  float2 br[kBias ? kVecs : 1][4];
+  float2 wr[kCols][4];
+  float2 br[kBias ? kCols : 1][4];
 #pragma unroll
-  for (int k = 0; k < kVecs; ++k) {
+  for (int k = 0; k < kCols; ++k) {
     const int64_t c = slice_elt0 + static_cast<int64_t>(gl + k * G) * 8;
 #pragma unroll
     for (int i = 0; i < 4; ++i) wr[k][i] = splat2(1.f);
@@ -455,8 +458,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       const float2 r2 = splat2(rstd);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        if constexpr (kBias) y[i] = fma2(mul2(h[i], r2), wr[k][i], br[kBias ? k : 0][i]);
-        else y[i] = mul2(mul2(h[i], r2), wr[k][i]);
+        if constexpr (kBias) y[i] = fma2(mul2(h[i], r2), wr[k % kCols][i], br[kBias ? k % kCols : 0][i]);
+        else y[i] = mul2(mul2(h[i], r2), wr[k % kCols][i]);
       }
       Pair8<OT>::store(op, y);
     } else {
@@ -468,10 +471,10 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       if constexpr (kRO) Vec8<ROe>::store(rop, h);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float2 w2 = wr[k][e >> 1];
+        const float2 w2 = wr[k % kCols][e >> 1];
         const float w = (e & 1) ? w2.y : w2.x;
         if constexpr (kBias) {
-          const float2 b2 = br[kBias ? k : 0][e >> 1];
+          const float2 b2 = br[kBias ? k % kCols : 0][e >> 1];
           y[e] = fmaf(h[e] * rstd, w, (e & 1) ? b2.y : b2.x);
         } else {
           y[e] = (h[e] * rstd) * w;
@@ -527,8 +530,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float2 xh = mul2(add2(h[i], nm), r2);
-      if constexpr (kBias) y[i] = fma2(xh, wr[k][i], br[kBias ? k : 0][i]);
-      else y[i] = mul2(xh, wr[k][i]);
+      if constexpr (kBias) y[i] = fma2(xh, wr[k % kCols][i], br[kBias ? k % kCols : 0][i]);
+      else y[i] = mul2(xh, wr[k % kCols][i]);
     }
     Pair8<OT>::store(op, y);
   };
@@ -567,7 +570,77 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
     }
   };
 
-  if (active_warp && ln_rows) {
+  if constexpr (kCols < kVecs) {
+    // --------- per-head column mode: kVecs / kCols super-rows per thread per sweep ---------
+    // Thread vector k is column k % kCols (vector gl + (k % kCols) * G of the super-row) of
+    // tile row sweep + gid + (k / kCols) * rps: the thread keeps the weight / bias of only
+    // kCols columns in registers, and one transposed segment reduction serves all kVecs
+    // (row, head) pairs. The planner picks this mode for per-head rows of at most
+    // kCols * T vectors; every tile row is a whole super-row (P = 1).
+    constexpr int kRpt = kVecs / kCols;
+    if (active_warp) {
+      int s = 0;
+      uint32_t ph = 0;
+      const int rstep = pl.rps * kRpt;
+      for (int64_t q = 0; q < n_local; ++q) {
+        const int64_t tile = cid + q * ncl;
+        mbar_wait(&L.full[s], ph, kSiteFwdFull);
+        const X* xs0 = stage_x(s);
+        const RTe* rs0 = stage_r(s);
+        const int64_t row0 = tile * pl.R;
+        const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
+        for (int sw = 0; sw < pl.R; sw += rstep) {
+          const int lr0 = sw + gid;
+          const bool active = in_group && lr0 < rows;
+          const unsigned amask = __ballot_sync(0xffffffffu, active);
+          if (!active) continue;
+          unsigned ok = 0;  // vectors whose column is in the slice and whose row is in the tile
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k)
+            if (((vmask >> k) & 1u) && lr0 + (k / kCols) * pl.rps < rows) ok |= 1u << k;
+          auto xoff = [&](int k) { return (lr0 + (k / kCols) * pl.rps) * xs_stride + (k % kCols) * G8; };
+          float part[kVecs];
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) part[k] = ((ok >> k) & 1u) ? sumsq(xs0 + xoff(k), rs0 + xoff(k)) : 0.f;
+          float rstd_k[kVecs];
+          seg_reduce<kVecs>(part, rstd_k, pl.vs, amask, [&](float t) { return rsqrtf(fmaf(t, inv_n, p.eps)); });
+          const int64_t g0 = (row0 + lr0) * pl.W + slice_elt0 + gl * 8;
+          OT* op = static_cast<OT*>(p.out) + g0;
+          ROe* rop = static_cast<ROe*>(p.ro) + g0;
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) {
+            if ((ok >> k) & 1u) {
+              const int64_t o = static_cast<int64_t>((k / kCols) * pl.rps) * pl.W + (k % kCols) * G8;
+              emit(xs0 + xoff(k), rs0 + xoff(k), op + o, rop + o, rstd_k[k], k);
+            }
+          }
+          // rstd per (row, head): lane i < kVecs of each segment stores the segment's value
+          // i, so one store instruction per sweep writes them all (the segment's lanes agree
+          // on which of its vectors are valid)
+          if (p.rstd != nullptr) {
+            const int i = gl & (pl.vs - 1);
+            if (pl.vs >= kVecs) {
+              if (i < kVecs && ((ok >> i) & 1u)) {
+                float v = rstd_k[0];
+#pragma unroll
+                for (int k = 1; k < kVecs; ++k)
+                  if (i == k) v = rstd_k[k];
+                p.rstd[(row0 + lr0 + (i / kCols) * pl.rps) * pl.heads + ((gl + (i % kCols) * G) >> pl.vs_shift)] = v;
+              }
+            } else if (i == 0) {
+#pragma unroll
+              for (int k = 0; k < kVecs; ++k)
+                if ((ok >> k) & 1u)
+                  p.rstd[(row0 + lr0 + (k / kCols) * pl.rps) * pl.heads + ((gl + (k % kCols) * G) >> pl.vs_shift)] =
+                      rstd_k[k];
+            }
+          }
+        }
+        if (release_slot(L, s, nwarps) && q + S < n_local) issue_unit(q + S, s);
+        if (++s == S) { s = 0; ph ^= 1u; }
+      }
+    }
+  } else if (active_warp && ln_rows) {
     // --------- LayerNorm rows, pipelined one tile deep (tiles hold one row per group) ---------
     // Iteration q: A(q) = sum of row q, posted; C(q-1) = output of row q-1 once its
     // variance is in; B(q) = squared deviations of row q once its mean is in, posted.

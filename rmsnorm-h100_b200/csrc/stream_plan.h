@@ -16,7 +16,8 @@ namespace rmsb200 {
 //               clusters of P CTAs would leave SMs idle -- P CTAs of one cooperative grid
 //               that exchange them through tagged records in global memory.
 //   tile      : R consecutive super-rows staged into one shared-memory stage by TMA.
-//   sweep     : rps super-rows processed concurrently by rps thread groups of G threads.
+//   sweep     : rps super-rows processed concurrently by rps thread groups of G threads
+//               (rps * kVecs / cols super-rows in per-head column mode).
 struct StreamPlan {
   int32_t T;          // threads of the CTA (multiple of 32); thread 0 also issues the copies
   int32_t G;          // consumer threads per super-row
@@ -38,6 +39,9 @@ struct StreamPlan {
   int32_t pipe_rows;  // RMSNorm row mode: rows pipelined one tile deep (ring holds one more slot)
   int32_t lag;        // rows the cluster exchange lags pass 1 by (P > 1): pass 2 of row i-lag
                       // follows pass 1 of row i
+  int32_t cols;       // thread vectors (columns) per super-row in a sweep: the kernel's vectors
+                      // per thread, or fewer in per-head column mode (each thread then covers
+                      // kVecs / cols super-rows of the sweep)
   int64_t nrows;      // super-rows
   int64_t ntiles;
   int64_t W;          // super-row width in elements (H * N)

@@ -127,6 +127,30 @@ def test_fwd_per_head(H, N, dtype, path):
     _fwd_case(H * 5, N, dtype, H=H, weight=True, residual="same", residual_dtype=F32)
 
 
+@pytest.mark.parametrize("H,N,dtype,tokens,cols", [
+    (32, 128, F16, 37, "cols=1"),     # 4096-wide super-rows, ragged last tile
+    (32, 128, BF16, 4099, "cols=1"),  # many tiles per CTA
+    (32, 256, BF16, 21, "cols=2"),    # 8192-wide: two columns per thread
+    (64, 128, F32, 9, "cols=2"),
+    (8, 64, F32, 45, "cols=1"),       # 512-wide: eight groups of 64 threads
+    (3, 256, F16, 29, "cols=1"),      # groups of 96 threads straddle warps
+    (4, 16, BF16, 50, "cols=1"),      # segments of 2 lanes (fewer than the 4 values per thread)
+    (2, 8, F32, 33, "cols=1"),        # segments of 1 lane
+    (128, 128, F16, 5, "cols=4"),     # 16384-wide: four columns (the general kernel)
+])
+def test_fwd_per_head_column_mode(H, N, dtype, tokens, cols):
+    """Per-head forward in column mode (several super-rows per thread per sweep): affine
+    variants, rstd stored or not, ragged tiles."""
+    _fwd_case(tokens * H, N, dtype, H=H, bias=True, expect=cols)
+    _fwd_case(tokens * H, N, dtype, H=H, seed=7, expect=cols)
+    _fwd_case(tokens * H, N, dtype, H=H, weight=False, bias=True, store_rstd=False, seed=9, expect=cols)
+
+
+def test_fwd_per_head_column_mode_off(monkeypatch):
+    monkeypatch.setenv("RMSNORM_B200_COL_MODE", "0")
+    _fwd_case(37 * 32, 128, F16, H=32, bias=True, expect="cols=4")
+
+
 def test_fwd_output_and_affine_dtypes():
     _fwd_case(6, 1024, BF16, out_dtype=F32, expect="fwd_stream")
     _fwd_case(6, 1024, F32, out_dtype=BF16)
