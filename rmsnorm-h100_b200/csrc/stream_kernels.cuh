@@ -960,10 +960,13 @@ __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& 
 }
 
 // X: saved input dtype; DY: dout dtype; DXT: dx dtype; DROT: dresidual_out dtype (NoT =
-// none); DREST: dresidual dtype (NoT = not written); kRstdBulk: see bwd_issue.
+// none); DREST: dresidual dtype (NoT = not written); kRstdBulk: see bwd_issue; kCols <
+// kVecs: per-head column mode, as in the forward (the thread's weight and dweight / dbias
+// accumulators cover kCols columns).
 template <typename X, typename DY, typename DXT, typename DROT, typename DREST, bool kHasDb, int kVecs,
-          int kBlock, int kMinBlocks, bool kRstdBulk = false>
+          int kBlock, int kMinBlocks, bool kRstdBulk = false, int kCols = kVecs>
 __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const BwdParams p) {
+  static_assert(kVecs % kCols == 0, "column mode: whole rows per thread");
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr bool kDro = Present<DROT>::value;
   constexpr bool kDres = Present<DREST>::value;
@@ -1022,14 +1025,14 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   unsigned vmask = 0;
 #pragma unroll
   for (int k = 0; k < kVecs; ++k)
-    if (in_group && gl + k * G < pl.vslice) vmask |= 1u << k;
+    if (in_group && gl + (k % kCols) * G < pl.vslice) vmask |= 1u << k;
 
   // weight of the thread's columns and its dweight / dbias accumulators, as float pairs
-  float2 wr[kVecs][4];
-  float2 dw[kVecs][4];
-  float2 db[kHasDb ? kVecs : 1][4];
+  float2 wr[kCols][4];
+  float2 dw[kCols][4];
+  float2 db[kHasDb ? kCols : 1][4];
 #pragma unroll
-  for (int k = 0; k < kVecs; ++k) {
+  for (int k = 0; k < kCols; ++k) {
     const int64_t c = slice_elt0 + static_cast<int64_t>(gl + k * G) * 8;
 #pragma unroll
     for (int i = 0; i < 4; ++i) { wr[k][i] = splat2(1.f); dw[k][i] = splat2(0.f); }
@@ -1052,9 +1055,9 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float2 t = mul2(xv[i], dv[i]);
-      acc = fma2(t, wr[k][i], acc);
-      dw[k][i] = fma2(t, r2, dw[k][i]);
-      if constexpr (kHasDb) db[kHasDb ? k : 0][i] = add2(db[kHasDb ? k : 0][i], dv[i]);
+      acc = fma2(t, wr[k % kCols][i], acc);
+      dw[k % kCols][i] = fma2(t, r2, dw[k % kCols][i]);
+      if constexpr (kHasDb) db[kHasDb ? k % kCols : 0][i] = add2(db[kHasDb ? k % kCols : 0][i], dv[i]);
     }
     return (acc.x + acc.y) * r;
   };
@@ -1067,7 +1070,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     const float2 rr = splat2(r);
     const float2 nb = splat2(-(r * r) * c);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) g[i] = fma2(mul2(dv[i], wr[k][i]), rr, mul2(xv[i], nb));
+    for (int i = 0; i < 4; ++i) g[i] = fma2(mul2(dv[i], wr[k % kCols][i]), rr, mul2(xv[i], nb));
     if constexpr (kDro) {
       float2 a[4];
       Pair8<DROe>::load(ap, a);
@@ -1155,7 +1158,59 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     }
   };
 
-  if (active_warp && rows_pipe) {
+  if constexpr (kCols < kVecs) {
+    // --------- per-head column mode: kVecs / kCols super-rows per thread per sweep ---------
+    // (see the forward): thread vector k is column k % kCols of tile row
+    // sweep + gid + (k / kCols) * rps, with that (row, head)'s rstd from the staged block
+    if (active_warp) {
+      int s = 0;
+      uint32_t ph = 0;
+      const int rstep = pl.rps * (kVecs / kCols);
+      for (int64_t q = 0; q < n_local; ++q) {
+        const int64_t tile = cid + q * ncl;
+        mbar_wait(&L.full[s], ph, kSiteBwdFull);
+        const int64_t row0 = tile * pl.R;
+        const int rows = static_cast<int>(min(static_cast<int64_t>(pl.R), pl.nrows - row0));
+        const RowPtrs rp = row_ptrs(s, 0);
+        for (int sw = 0; sw < pl.R; sw += rstep) {
+          const int lr0 = sw + gid;
+          const bool active = in_group && lr0 < rows;
+          const unsigned amask = __ballot_sync(0xffffffffu, active);
+          if (!active) continue;
+          unsigned ok = 0;  // vectors whose column is in the slice and whose row is in the tile
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k)
+            if (((vmask >> k) & 1u) && lr0 + (k / kCols) * pl.rps < rows) ok |= 1u << k;
+          auto eoff = [&](int k) { return (lr0 + (k / kCols) * pl.rps) * x_stride + (k % kCols) * G8; };
+          float part[kVecs], rstd_k[kVecs], c_k[kVecs];
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) {
+            part[k] = 0.f;
+            rstd_k[k] = 0.f;
+            if ((ok >> k) & 1u) {
+              const float r = rp.rstd[(lr0 + (k / kCols) * pl.rps) * rstd_per_row +
+                                      ((gl + (k % kCols) * G) >> pl.vs_shift)];
+              rstd_k[k] = r;
+              part[k] = dot_acc(rp.x + eoff(k), rp.dy + eoff(k), r, k);
+            }
+          }
+          seg_reduce<kVecs>(part, c_k, pl.vs, amask, [&](float t) { return t * inv_n; });
+          const int64_t g0 = (row0 + lr0) * pl.W + slice_elt0 + gl * 8;
+          DXT* dxp = static_cast<DXT*>(p.dx) + g0;
+          DRESe* drp = static_cast<DRESe*>(p.dres) + g0;
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) {
+            if ((ok >> k) & 1u) {
+              const int64_t o = static_cast<int64_t>((k / kCols) * pl.rps) * pl.W + (k % kCols) * G8;
+              dx_emit(rp.x + eoff(k), rp.dy + eoff(k), rp.dro + eoff(k), dxp + o, drp + o, rstd_k[k], c_k[k], k);
+            }
+          }
+        }
+        if (release_slot(L, s, nwarps) && q + S < n_local) issue_unit(q + S, s);
+        if (++s == S) { s = 0; ph ^= 1u; }
+      }
+    }
+  } else if (active_warp && rows_pipe) {
     // --------- rows pipelined one tile deep ---------
     // Iteration q: dot products (and dweight / dbias) of row q, posted; dx of row q-1
     // once its dot product is in.
@@ -1301,7 +1356,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   // Every owned column is written, zeros included, so the reduction reads no stale data.
   const int64_t pbase = (cid * pl.rps + gid) * pl.W + slice_elt0 + gl * 8;
 #pragma unroll
-  for (int k = 0; k < kVecs; ++k) {
+  for (int k = 0; k < kCols; ++k) {
     if ((vmask >> k) & 1u) {
       if (p.dw_part != nullptr) Pair8<float>::store(p.dw_part + pbase + k * G8, dw[k]);
       if constexpr (kHasDb) {

@@ -258,6 +258,33 @@ def test_bwd_per_head(H, N, dtype):
     _bwd_case(H * 7, N, dtype, H=H, has_bias=True)
 
 
+@pytest.mark.parametrize("H,N,dtype,tokens,cols", [
+    (32, 128, F16, 37, "cols=1"),     # ragged last tile
+    (32, 128, BF16, 2051, "cols=1"),  # many tiles per CTA (dweight / dbias over many rows)
+    (32, 256, BF16, 21, "cols=2"),
+    (64, 128, BF16, 9, "cols=2"),
+    (64, 128, F32, 9, None),          # fp32: one column tile (2 rows) fills shared memory alone
+    (8, 64, BF16, 45, "cols=1"),      # 32 rows per sweep
+    (8, 64, F32, 45, None),           # fp32: one 32-row column tile fills shared memory alone
+    (3, 256, F16, 29, "cols=1"),      # groups of 96 threads straddle warps
+    (4, 16, BF16, 50, "cols=1"),      # segments of 2 lanes
+    (2, 8, F16, 333, "cols=1"),       # segments of 1 lane, 1024 rows per sweep
+])
+def test_bwd_per_head_column_mode(H, N, dtype, tokens, cols):
+    """Per-head backward in column mode: dweight / dbias accumulated over several rows per
+    thread per sweep, the per-(row, head) rstd read from the staged block."""
+    _bwd_case(tokens * H, N, dtype, H=H, has_bias=True, expect=cols)
+    _bwd_case(tokens * H, N, dtype, H=H, seed=7, expect=cols)
+    # without a per-head weight the rows are plain N-wide rows (no column mode)
+    _bwd_case(tokens * H, N, dtype, H=H, weight=False, has_bias=True, seed=9)
+
+
+def test_bwd_per_head_column_mode_off(monkeypatch):
+    monkeypatch.setenv("RMSNORM_B200_COL_MODE", "0")
+    plan = _bwd_case(37 * 32, 128, F16, H=32, has_bias=True)
+    assert "cols=1" not in plan, plan
+
+
 def test_bwd_mixed_dtypes_prenorm():
     # saved x is an fp32 residual_out, dout is half/bf16: the prenorm-with-fp32-residual case
     for dy in (F16, BF16):
