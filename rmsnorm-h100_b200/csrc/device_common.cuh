@@ -41,6 +41,14 @@ __device__ __forceinline__ void record_error(int code, int where) {
   }
 }
 
+// Programmatic dependent launch. pdl_wait: blocks until the grids this launch depends on
+// have completed and their memory operations are visible (a no-op for a launch without
+// the programmatic-serialization attribute); every global access of a streaming kernel
+// follows it. pdl_launch_dependents: lets the next launch in the stream be scheduled
+// (its CTAs then run their shared-memory prologue as this grid's CTAs retire).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ bool abort_requested() {
   return *reinterpret_cast<volatile int*>(&g_status) != 0;
 }

@@ -452,7 +452,13 @@ int launch_stream(DeviceState* ds, void (*kernel)(const Params), Params params, 
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
-  if (pl.P > 1 && pl.xmode == kXCluster) {
+  if (pl.P == 1 && env_int("RMSNORM_B200_PDL", 1)) {
+    // programmatic dependent launch: the grid may be scheduled while the previous kernel
+    // in the stream retires; the kernel waits for it before its first global access
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 1;
+  } else if (pl.P > 1 && pl.xmode == kXCluster) {
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = pl.P;
     attr[0].val.clusterDim.y = 1;

@@ -373,6 +373,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
   // RMSNorm row mode pipelined the same way (one reduction) when the planner asked for it
   const bool rms_rows = !kLNMode && pl.pipe_rows && !pl.seg_mode && pl.P == 1 && pl.R == pl.rps && pl.S >= 3;
   init_barriers(L, pl, ln_rows || rms_rows);
+  pdl_wait();  // every global access of the launch follows this point
+  pdl_launch_dependents();
 
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const uint64_t pol = l2_policy_evict_first();
@@ -995,6 +997,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   // row mode with one row per group per tile: rows pipelined one tile deep (when planned)
   const bool rows_pipe = pl.pipe_rows && !pl.seg_mode && pl.P == 1 && pl.R == pl.rps && pl.S >= 3;
   init_barriers(L, pl, rows_pipe);
+  pdl_wait();  // every global access of the launch follows this point
+  pdl_launch_dependents();
 
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const int rstd_per_row = pl.seg_mode ? pl.heads : 1;
