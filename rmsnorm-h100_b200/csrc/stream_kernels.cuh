@@ -439,15 +439,17 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       for (int i = 1; i < 4; ++i) acc = fma2(h[i], h[i], acc);
       return acc.x + acc.y;
     } else {
-      float h[8], r[8];
+      float h[8];
       Vec8<X>::load(xp, h);
-      Vec8<RTe>::load(rp, r);
+      if constexpr (kRes) {  // the stage holds a residual slice only when there is a residual
+        float r[8];
+        Vec8<RTe>::load(rp, r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[e] += r[e];
+      }
       float acc = 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        h[e] += r[e];
-        acc = fmaf(h[e], h[e], acc);
-      }
+      for (int e = 0; e < 8; ++e) acc = fmaf(h[e], h[e], acc);
       return acc;
     }
   };
@@ -465,11 +467,14 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       }
       Pair8<OT>::store(op, y);
     } else {
-      float h[8], r[8], y[8];
+      float h[8], y[8];
       Vec8<X>::load(xp, h);
-      Vec8<RTe>::load(rp, r);
+      if constexpr (kRes) {
+        float r[8];
+        Vec8<RTe>::load(rp, r);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) h[e] += r[e];
+        for (int e = 0; e < 8; ++e) h[e] += r[e];
+      }
       if constexpr (kRO) Vec8<ROe>::store(rop, h);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
