@@ -13,6 +13,9 @@
 //   * threads read 8-element vectors from shared memory and reduce each row:
 //       - per-head rows of up to 32 vectors ("seg" mode): xor shuffles inside a lane
 //         segment, transposed so a thread's values for several heads share the levels;
+//         per-head super-rows of up to 2 x T vectors run in column mode (kCols < kVecs:
+//         a thread owns 1-2 vector columns across several super-rows of the sweep, so
+//         fewer weight / bias / dweight registers stay live);
 //       - whole rows ("row" mode): warp shuffles and one named barrier per row group, or,
 //         for pipelined rows, split-phase reductions through per-group mbarriers so the
 //         output pass of the previous row hides the wait (LayerNorm always, RMSNorm
@@ -22,6 +25,8 @@
 //         groups of a cooperative grid) and every warp sums the P totals; pass 1 of row i
 //         and its exchange overlap pass 2 of row i - lag;
 //     then they re-read the slot and write outputs with 16-byte streaming stores;
+//   * every launch waits (griddepcontrol.wait) before its first global access, so it may
+//     be launched as a programmatic dependent of the previous kernel in the stream;
 //   * every per-element dtype, the bias and the LayerNorm mode are template parameters
 //     (absent tensors are `NoT`), so the inner loops carry no runtime type dispatch; the
 //     arithmetic uses sm_100's paired fp32 instructions where that measured faster;
