@@ -169,52 +169,71 @@ __global__ void __launch_bounds__(kGenericThreads) bwd_generic_partials_kernel(
 }
 
 // out[j] = sum over partial rows c < C and heads h < fold of part[c][h * N + j], in a fixed
-// order: warp w of the block sums rows c = w, w + 8, w + 16, ... (heads innermost), then
-// the 8 warp sums are added in warp order. fold = H folds a per-head super-row back onto a
-// shared [N] parameter; fold = 1 keeps all W = H*N columns. One lane per column (32
-// columns per block), so every warp load is a coalesced 128-byte row segment.
+// order: warp w of the block sums rows c = w, w + 16, w + 32, ... (eight rows' loads in
+// flight per step, added in row order; heads innermost), then the 16 warp sums are added in
+// warp order. fold = H folds a per-head super-row back onto a shared [N] parameter; fold = 1
+// keeps all W = H*N columns. One lane per column (32 columns per block), so every warp load
+// is a coalesced 128-byte row segment. blockIdx.y selects the job (dweight, dbias), so one
+// launch reduces both. Narrow rows (per-head backwards: 1024-4096 columns, 148-600 partial
+// rows) have few column blocks, so the rows are spread over 16 warps with eight loads in
+// flight each, which keeps the number of dependent memory round trips per warp small.
 constexpr int kReduceCols = 32;
-constexpr int kReduceWarps = 8;
+constexpr int kReduceWarps = 16;
 constexpr int kReduceThreads = kReduceCols * kReduceWarps;
+constexpr int kReduceUnroll = 8;
 
-__global__ void __launch_bounds__(kReduceThreads) reduce_partials_kernel(
-    const float* __restrict__ part, int64_t C, int64_t W, int64_t N, int32_t fold, void* out,
-    int32_t out_dt) {
+struct ReduceJob {
+  const float* part;  // [C][W] partial rows
+  void* out;          // [wout]
+  int64_t wout;       // output columns: N when heads are folded, else W
+  int32_t fold;       // heads summed into each output column (1 = none)
+  int32_t out_dt;
+};
+
+struct ReduceParams {
+  ReduceJob job[2];
+  int64_t C;  // partial rows
+  int64_t W;  // columns of a partial row (H * N)
+  int64_t N;  // columns of one head
+};
+
+__global__ void __launch_bounds__(kReduceThreads) reduce_partials_kernel(const ReduceParams p) {
   __shared__ float acc_w[kReduceWarps][kReduceCols];
+  const ReduceJob& jb = blockIdx.y == 0 ? p.job[0] : p.job[1];  // no dynamic index into the parameters
+  if (static_cast<int64_t>(blockIdx.x) * kReduceCols >= jb.wout) return;  // whole block idle
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int64_t wout = fold > 1 ? N : W;
   const int64_t j = static_cast<int64_t>(blockIdx.x) * kReduceCols + lane;
   float acc = 0.f;
-  if (j < wout) {
+  if (j < jb.wout) {
+    const float* col = jb.part + j;
     int64_t c = warp;
+    if (jb.fold == 1) {
 #pragma unroll 1
-    for (; c + 3 * kReduceWarps < C; c += 4 * kReduceWarps) {
-      // four rows per step: independent loads in flight, added in row order
-      float v[4];
+      for (; c + (kReduceUnroll - 1) * kReduceWarps < p.C; c += kReduceUnroll * kReduceWarps) {
+        float v[kReduceUnroll];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float* row = part + (c + u * kReduceWarps) * W + j;
-        float t = 0.f;
-        for (int h = 0; h < fold; ++h) t += row[h * N];
-        v[u] = t;
+        for (int u = 0; u < kReduceUnroll; ++u) v[u] = col[(c + u * kReduceWarps) * p.W];
+#pragma unroll
+        for (int u = 0; u < kReduceUnroll; ++u) acc += v[u];
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) acc += v[u];
-    }
-    for (; c < C; c += kReduceWarps) {
-      const float* row = part + c * W + j;
-      float t = 0.f;
-      for (int h = 0; h < fold; ++h) t += row[h * N];
-      acc += t;
+      for (; c < p.C; c += kReduceWarps) acc += col[c * p.W];
+    } else {
+      for (; c < p.C; c += kReduceWarps) {
+        const float* row = col + c * p.W;
+        float t = 0.f;
+        for (int h = 0; h < jb.fold; ++h) t += row[h * p.N];
+        acc += t;
+      }
     }
   }
   acc_w[warp][lane] = acc;
   __syncthreads();
-  if (warp == 0 && j < wout) {
+  if (warp == 0 && j < jb.wout) {
     float t = 0.f;
+#pragma unroll
     for (int w = 0; w < kReduceWarps; ++w) t += acc_w[w][lane];
-    store1_rt(out, out_dt, j, t);
+    store1_rt(jb.out, jb.out_dt, j, t);
   }
 }
 

@@ -988,24 +988,29 @@ int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream
     t_last_plan = "bwd empty";
   }
 
-  const int64_t nparts = a->rows > 0 ? bp.nparts : 0;
-  auto reduce = [&](const float* part, void* outp, int out_dt, int out_heads) -> int {
-    const int fold = (out_heads == 1 && a->heads > 1) ? a->heads : 1;
-    const int64_t wout = fold > 1 ? a->hidden : bp.W;
-    const unsigned blocks = static_cast<unsigned>((wout + kReduceCols - 1) / kReduceCols);
-    reduce_partials_kernel<<<blocks, kReduceThreads, 0, stream>>>(part, nparts, bp.W, a->hidden, fold,
-                                                                 outp, out_dt);
+  // dweight and dbias: fixed-order column sums of the partial rows, one launch for both
+  ReduceParams rp = {};
+  rp.C = a->rows > 0 ? bp.nparts : 0;
+  rp.W = bp.W;
+  rp.N = a->hidden;
+  int njobs = 0;
+  int64_t max_wout = 0;
+  auto add_job = [&](const float* part, void* outp, int out_dt, int out_heads) {
+    ReduceJob& jb = rp.job[njobs++];
+    jb.fold = (out_heads == 1 && a->heads > 1) ? a->heads : 1;
+    jb.wout = jb.fold > 1 ? a->hidden : bp.W;
+    jb.part = part;
+    jb.out = outp;
+    jb.out_dt = out_dt;
+    max_wout = std::max(max_wout, jb.wout);
+  };
+  if (a->dweight) add_job(dw_part, a->dweight, a->dweight_dtype, a->weight_heads);
+  if (a->dbias) add_job(db_part, a->dbias, a->dbias_dtype, a->dbias_heads);
+  if (njobs > 0) {
+    const dim3 grid(static_cast<unsigned>((max_wout + kReduceCols - 1) / kReduceCols), static_cast<unsigned>(njobs));
+    reduce_partials_kernel<<<grid, kReduceThreads, 0, stream>>>(rp);
     if (cudaGetLastError() != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
     g_launches.fetch_add(1, std::memory_order_relaxed);
-    return RMSNORM_B200_OK;
-  };
-  if (a->dweight) {
-    st = reduce(dw_part, a->dweight, a->dweight_dtype, a->weight_heads);
-    if (st) return st;
-  }
-  if (a->dbias) {
-    st = reduce(db_part, a->dbias, a->dbias_dtype, a->dbias_heads);
-    if (st) return st;
   }
   return RMSNORM_B200_OK;
 }
