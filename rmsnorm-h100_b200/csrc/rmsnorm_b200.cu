@@ -57,6 +57,7 @@ struct DeviceState {
   int sm_count = 0;
   void* noalloc_scratch = nullptr;  // device address of g_noalloc_scratch on this device
   XRecord* xrec = nullptr;          // device address of g_xrec on this device
+  uint32_t* xgen = nullptr;         // device address of g_xgen on this device
   uint32_t xepoch = 0;              // launches that used the global-memory exchange
   std::mutex mu;
   std::map<const void*, bool> attrs_done;
@@ -101,26 +102,31 @@ int noalloc_scratch(DeviceState* ds, void** out) {
 }
 
 // Records of the global-memory row-total exchange (split rows on a cooperative grid): a
-// file-scope device array, kXRecSets sets used round-robin by launch epoch, so launches
-// that overlap at their ends (at most a few on one device) use different sets; a record
-// whose tag carries another epoch (31 bits) is never taken for this launch's.
+// file-scope device array, kXRecSets sets used round-robin by launch, so launches that
+// overlap at their ends (at most a few on one device) use different sets. Each set has
+// one generation counter per CTA group; every execution of a launch draws a fresh
+// generation from it on the device and tags its records with it, so neither an earlier
+// launch nor an earlier replay of the same captured launch can supply a record.
 static __device__ XRecord g_xrec[kXRecSets * kXRecMaxCtas * kXSlots];
+static __device__ uint32_t g_xgen[kXRecSets * kXRecMaxCtas];
 
-// Next launch epoch (never 0, so zero-initialised records never match) and its record set.
-int next_xepoch(DeviceState* ds, XRecord** rec, uint32_t* epoch) {
+// Next record set (round robin) and its generation counters.
+int next_xset(DeviceState* ds, XRecord** rec, uint32_t** gen) {
   std::lock_guard<std::mutex> lock(ds->mu);
   if (!ds->xrec) {
     void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_xrec) != cudaSuccess || !ptr) {
+    void* gptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_xrec) != cudaSuccess || !ptr ||
+        cudaGetSymbolAddress(&gptr, g_xgen) != cudaSuccess || !gptr) {
       cudaGetLastError();
       return RMSNORM_B200_ERR_CUDA;
     }
     ds->xrec = static_cast<XRecord*>(ptr);
+    ds->xgen = static_cast<uint32_t*>(gptr);
   }
-  ds->xepoch = (ds->xepoch + 1) & 0x7fffffffu;  // the tag keeps 31 bits of the epoch
-  if (ds->xepoch == 0) ds->xepoch = 1;
-  *epoch = ds->xepoch;
-  *rec = ds->xrec + static_cast<size_t>(ds->xepoch % kXRecSets) * kXRecMaxCtas * kXSlots;
+  const uint32_t set = ds->xepoch++ % kXRecSets;
+  *rec = ds->xrec + static_cast<size_t>(set) * kXRecMaxCtas * kXSlots;
+  *gen = ds->xgen + static_cast<size_t>(set) * kXRecMaxCtas;
   return RMSNORM_B200_OK;
 }
 
@@ -445,8 +451,8 @@ int launch_stream(DeviceState* ds, void (*kernel)(const Params), Params params, 
   if (grid_out) *grid_out = grid;
   if (dry_run) return RMSNORM_B200_OK;
   params.xrec = nullptr;
-  params.xepoch = 0;
-  if (pl.xmode == kXGlobal && next_xepoch(ds, &params.xrec, &params.xepoch) != RMSNORM_B200_OK)
+  params.xgen = nullptr;
+  if (pl.xmode == kXGlobal && next_xset(ds, &params.xrec, &params.xgen) != RMSNORM_B200_OK)
     return RMSNORM_B200_ERR_CUDA;
   params.pl = pl;
   cudaLaunchConfig_t cfg = {};

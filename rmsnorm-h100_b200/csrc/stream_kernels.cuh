@@ -52,6 +52,16 @@ constexpr int kMaxLag = 3;  // deepest exchange lag the slots allow: kXSlots >= 
 
 constexpr int kGroupRed = 4;  // split-phase reductions per row group: 2 statistics x 2 rows in flight
 
+// Dynamic shared memory (every extern __shared__ array aliases its start): the S ring
+// stages, then the barrier / reduction area laid out by carve_smem.
+extern __shared__ __align__(128) unsigned char rmsb_dyn_smem[];
+
+// Byte offset, within the area after the stages, of the global-memory exchange's tag base
+// (after full, xbar, xpart, red, done, gbar and gpart).
+constexpr uint32_t kXTagOff = kMaxStages * 8 + kXSlots * 8 + kXSlots * kMaxCluster * 4 + 64 * 4 + kMaxStages * 4 +
+                              16 * kGroupRed * 8 + kGroupRed * 16 * 4;
+static_assert(kXTagOff + 4 <= kSmemReserve, "barrier area exceeds its reserve");
+
 struct SmemLayout {
   uint64_t* full;   // [kMaxStages] slot filled
   uint64_t* xbar;   // [kXSlots] cluster exchange barriers
@@ -60,6 +70,7 @@ struct SmemLayout {
   int* done;        // [kMaxStages] warps finished with the slot's current tile
   uint64_t* gbar;   // [16 groups][kGroupRed] split-phase row-group reductions (LayerNorm)
   float* gpart;     // [kGroupRed][16 warps] their per-warp partials
+  uint32_t* xgen;   // [1] the execution generation of the global-memory exchange
 };
 
 __device__ __forceinline__ SmemLayout carve_smem(unsigned char* smem, const StreamPlan& pl) {
@@ -72,6 +83,7 @@ __device__ __forceinline__ SmemLayout carve_smem(unsigned char* smem, const Stre
   L.done = reinterpret_cast<int*>(L.red + 64);
   L.gbar = reinterpret_cast<uint64_t*>(L.done + kMaxStages);
   L.gpart = reinterpret_cast<float*>(L.gbar + 16 * kGroupRed);
+  L.xgen = reinterpret_cast<uint32_t*>(tail + kXTagOff);
   return L;
 }
 
@@ -167,14 +179,39 @@ __device__ __forceinline__ float group_take(const StreamPlan& pl, const SmemLayo
 // totals with the same shuffle tree as above. The slot argument above covers the records:
 // with lag <= kMaxLag a CTA rewrites its record for row r only after every warp of every
 // peer has read its row r - kXSlots, so a reader finds row r's word or row r - kXSlots's.
+// Across executions: records are never cleared, so every execution tags its words with a
+// generation of its own (xgen_begin). A host-side value baked into the launch parameters
+// would not do: a CUDA graph replays the same parameters, and a reader running ahead of its
+// peer would then take the previous replay's word for the same row as this one's.
 struct XCtx {
   XRecord* rec;      // this launch's record set
-  uint32_t epoch2;   // launch epoch << 1
   int64_t cta0;      // first CTA of the group
 };
 
-__device__ __forceinline__ uint32_t xrec_tag(const XCtx& xc, uint32_t seq) {
-  return xc.epoch2 | ((seq / kXSlots) & 1u);
+// Tag of row `seq`: the execution's tag base (0x80000000 | generation << 1, stored in
+// shared memory by xgen_begin and addressed from the plan, so no register holds it across
+// the kernel) | bit 0 of seq / kXSlots.
+__device__ __forceinline__ uint32_t xrec_tag(const StreamPlan& pl, uint32_t seq) {
+  const uint32_t base =
+      *reinterpret_cast<const uint32_t*>(rmsb_dyn_smem + static_cast<size_t>(pl.S) * pl.stage_bytes + kXTagOff);
+  return base | ((seq / kXSlots) & 1u);
+}
+
+// Draws this execution's generation for CTA group `cid` (kXGlobal; every thread of the
+// CTA calls it, after pdl_wait). Each of the group's P CTAs adds kMaxCluster / P to the
+// group's counter, so every execution adds exactly kMaxCluster whatever its P, and the P
+// CTAs of one execution all read old values in [g * kMaxCluster, (g + 1) * kMaxCluster):
+// the same generation g, with no wait among them. This holds as long as two executions
+// that share a record set and a group do not run at the same time on the GPU (launches of
+// one stream never do; the host hands consecutive launches different record sets).
+// The tag base is kept in shared memory (not in a register for the whole kernel).
+__device__ __forceinline__ void xgen_begin(const StreamPlan& pl, const SmemLayout& L, uint32_t* xgen, int64_t cid) {
+  if (pl.P <= 1 || pl.xmode != kXGlobal) return;
+  if (threadIdx.x == 0) {
+    const uint32_t g = atomicAdd(xgen + cid, static_cast<uint32_t>(kMaxCluster / pl.P)) / kMaxCluster;
+    *L.xgen = 0x80000000u | ((g & 0x3fffffffu) << 1);
+  }
+  __syncthreads();
 }
 
 __device__ __forceinline__ XRecord xrec_load(const StreamPlan& pl, const XCtx& xc, int lane, uint32_t seq) {
@@ -189,7 +226,7 @@ __device__ __forceinline__ void cluster_send(float v, const StreamPlan& pl, cons
   if (pl.xmode == kXGlobal) {
     if (lane == 0)
       st_relaxed_u64(xc.rec + (xc.cta0 + rank) * kXSlots + slot,
-                     (static_cast<unsigned long long>(xrec_tag(xc, seq)) << 32) | __float_as_uint(v));
+                     (static_cast<unsigned long long>(xrec_tag(pl, seq)) << 32) | __float_as_uint(v));
     return;
   }
   float* xp = L.xpart + slot * kMaxCluster;
@@ -206,7 +243,7 @@ __device__ __forceinline__ float cluster_recv(const StreamPlan& pl, const SmemLa
                                               uint32_t seq, XRecord pre, int site) {
   const uint32_t slot = seq & (kXSlots - 1);
   if (pl.xmode == kXGlobal) {
-    const uint32_t want = xrec_tag(xc, seq);
+    const uint32_t want = xrec_tag(pl, seq);
     XRecord w = pre;
     uint64_t t0 = 0;
     while (!__all_sync(0xffffffffu, lane >= pl.P || static_cast<uint32_t>(w >> 32) == want)) {
@@ -370,7 +407,6 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       ncl = gridDim.x / pl.P;
     }
   }
-  const XCtx xc{p.xrec, p.xepoch << 1, cid * pl.P};
   constexpr bool kLNMode = kLN;
   // LayerNorm row mode: rows pipelined tile by tile (the planner gives one row per group
   // per tile and at least two slots)
@@ -380,6 +416,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
   init_barriers(L, pl, ln_rows || rms_rows);
   pdl_wait();  // every global access of the launch follows this point
   pdl_launch_dependents();
+  xgen_begin(pl, L, p.xgen, cid);
+  const XCtx xc{p.xrec, cid * pl.P};
 
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const uint64_t pol = l2_policy_evict_first();
@@ -1003,12 +1041,13 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
       ncl = gridDim.x / pl.P;
     }
   }
-  const XCtx xc{p.xrec, p.xepoch << 1, cid * pl.P};
   // row mode with one row per group per tile: rows pipelined one tile deep (when planned)
   const bool rows_pipe = pl.pipe_rows && !pl.seg_mode && pl.P == 1 && pl.R == pl.rps && pl.S >= 3;
   init_barriers(L, pl, rows_pipe);
   pdl_wait();  // every global access of the launch follows this point
   pdl_launch_dependents();
+  xgen_begin(pl, L, p.xgen, cid);
+  const XCtx xc{p.xrec, cid * pl.P};
 
   const int64_t slice_elt0 = static_cast<int64_t>(rank) * pl.vslice * 8;
   const int rstd_per_row = pl.seg_mode ? pl.heads : 1;

@@ -65,9 +65,11 @@ constexpr int kXGlobal = 1;
 
 // One row total of one CTA in the global-memory exchange, in one 64-bit word written and
 // read whole (single-copy atomic): high half = tag, low half = the float's bits. Tag =
-// (launch epoch << 1) | (bit 0 of row / kXSlots): a reader waiting for a row finds either
-// that row's word or the one of the row kXSlots before it in the same record, or a word
-// of an earlier launch (another epoch).
+// 0x80000000 | (execution generation << 1) | (bit 0 of row / kXSlots). The generation is
+// drawn on the device by every execution of the launch (a graph replay of the same launch
+// parameters draws a new one), so a reader waiting for a row finds that row's word, the
+// one of the row kXSlots before it, or a word of an earlier execution (another
+// generation); never-written records (zero) carry no valid tag.
 using XRecord = unsigned long long;
 constexpr int kXRecSets = 4;        // record sets, used round-robin by launch epoch
 constexpr int kXRecMaxCtas = 512;   // CTAs of a global-exchange grid
@@ -86,7 +88,7 @@ struct FwdParams {
   float eps;
   float* mean;     // LayerNorm: per-row mean (null = not stored)
   XRecord* xrec;   // kXGlobal: this launch's record set ([kXRecMaxCtas][kXSlots])
-  uint32_t xepoch; // kXGlobal: launch epoch (never 0 modulo 2^31)
+  uint32_t* xgen;  // kXGlobal: the set's generation counters, one per CTA group
 };
 
 struct BwdParams {
@@ -103,7 +105,7 @@ struct BwdParams {
   int32_t w_dt;
   int32_t w_per_head;
   XRecord* xrec;   // as in FwdParams
-  uint32_t xepoch;
+  uint32_t* xgen;
 };
 
 }  // namespace rmsb200

@@ -39,13 +39,18 @@ class HostPipeline:
             ]
         return self._bufs[key]
 
-    def _run(self, rows, ins: Dict[str, torch.Tensor], outs: Dict[str, torch.Tensor], launch, multiple=1):
+    def _run(self, rows, ins: Dict[str, torch.Tensor], outs: Dict[str, torch.Tensor], launch, multiple=1,
+             scratch: Optional[Dict[str, Tuple[tuple, torch.dtype]]] = None):
         """Generic chunk loop: copy `ins` rows in, call launch(buffer_set, nrows) on the
-        compute stream, copy `outs` rows back. Chunks hold a multiple of `multiple` rows."""
+        compute stream, copy `outs` rows back. Chunks hold a multiple of `multiple` rows.
+        `scratch` (name -> (trailing shape, dtype)) adds device-only buffers of `chunk` rows
+        to every buffer set (intermediates that never leave the device)."""
         cur = torch.cuda.current_stream(self.device)
         n = ins[next(iter(ins))].shape[-1]
         chunk = max(multiple, self.chunk_rows - self.chunk_rows % multiple)
         specs = {k: ((chunk, n), v.dtype) for k, v in {**ins, **outs}.items()}
+        for k, (tail, dt) in (scratch or {}).items():
+            specs[k] = ((chunk, *tail), dt)
         bufs = self._staging(("rows", n, tuple(sorted((k, str(v[1])) for k, v in specs.items()))), specs)
         h2d_done = [torch.cuda.Event() for _ in range(self.depth)]
         comp_done = [torch.cuda.Event() for _ in range(self.depth)]
@@ -176,3 +181,55 @@ class HostPipeline:
 
         self._run(rows, {"x": x, "dy": dout}, {"dx": dx}, launch, multiple=h)
         return dx, dw, db
+
+    def fwd_bwd(self, x: torch.Tensor, weight: Optional[torch.Tensor], bias: Optional[torch.Tensor],
+                residual: Optional[torch.Tensor], dout: torch.Tensor,
+                residual_dtype: Optional[torch.dtype] = None, eps: float = 1e-6,
+                out: Optional[torch.Tensor] = None, dx: Optional[torch.Tensor] = None,
+                grads: Optional[torch.Tensor] = None):
+        """Forward and backward of one training step on host tensors x / residual / dout
+        ([rows, N] with a shared (N,) weight / bias on the device; pinned for overlap).
+        Per chunk: the inputs are copied in, the forward writes out, residual_out and rstd
+        (residual_out and rstd stay in device buffers), the backward reads them with dout
+        and writes dx, and out / dx are copied back; dresidual is dx, as in rmsnorm_bwd with
+        has_residual. dweight / dbias are fp32 sums over all chunks on the device,
+        accumulated in chunk order (into `grads` = [dweight | dbias] fp32 when given).
+        Returns (out, dx, dweight, dbias)."""
+        rows, n = x.shape
+        if out is None:
+            out = torch.empty((rows, n), dtype=x.dtype, pin_memory=True)
+        if dx is None:
+            dx = torch.empty((rows, n), dtype=x.dtype, pin_memory=True)
+        nw = n if weight is not None else 0
+        nb = n if bias is not None else 0
+        if grads is None:
+            grads = torch.empty(nw + nb, dtype=torch.float32, device=self.device)
+        grads.zero_()
+        acc_w = grads[:nw] if nw else None
+        acc_b = grads[nw:nw + nb] if nb else None
+        part = torch.empty(nw + nb, dtype=torch.float32, device=self.device)
+        part_w = part[:nw] if nw else None
+        part_b = part[nw:nw + nb] if nb else None
+        w = weight.contiguous() if weight is not None else None
+        b = bias.contiguous() if bias is not None else None
+        ro_dt = residual_dtype or (residual.dtype if residual is not None else x.dtype)
+        ins = {"x": x, "dy": dout}
+        if residual is not None:
+            ins["res"] = residual
+        scratch = {"ro": ((n,), ro_dt), "rstd": ((), torch.float32)}
+
+        def launch(buf, m):
+            ro = buf["ro"][:m]
+            rstd = buf["rstd"][:m]
+            _lib.fwd(buf["x"][:m], buf["res"][:m] if "res" in buf else None, w, 1, b, 1, buf["out"][:m], ro,
+                     rstd, 1, float(eps))
+            a = _lib.bwd_args(ro, buf["dy"][:m], rstd, w, 1, None, buf["dx"][:m], None, part_w, part_b, 1, 1)
+            nbytes = _lib.bwd_workspace_bytes(a, self.device)
+            if self._ws is None or self._ws.numel() < nbytes:
+                self._ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=self.device)
+            _lib.bwd(a, self.device, self._ws)
+            if nw or nb:
+                grads.add_(part)
+
+        self._run(rows, ins, {"out": out, "dx": dx}, launch, multiple=1, scratch=scratch)
+        return out, dx, acc_w, acc_b

@@ -208,19 +208,23 @@ def _db_layout(bias, weight, x, h):
 
 
 def _bwd_cuda(x, weight, dout, rstd, dresidual_out, has_bias, has_residual, bias, h,
-              dx_dtype=None, dresidual_dtype=None):
+              dx_dtype=None, dresidual_dtype=None, dw_out=None, db_out=None):
+    """dw_out / db_out: caller buffers (any float dtype, the affine shapes) that receive
+    dweight / dbias instead of new tensors in the affine dtypes."""
     x_c = _contig(x)
     dout_c = _contig(dout)
     dro_c = _contig(dresidual_out)
     rstd_c = rstd.contiguous().reshape(-1)
     dx = torch.empty(x_c.shape, dtype=dx_dtype or x.dtype, device=x.device)
     w_c = _contig(weight)
-    dw = torch.empty(weight.shape, dtype=weight.dtype, device=x.device) if weight is not None else None
+    dw = None
+    if weight is not None:
+        dw = dw_out if dw_out is not None else torch.empty(weight.shape, dtype=weight.dtype, device=x.device)
     db = None
     db_heads = 1
     if has_bias:
         db_dtype, db_shape, db_heads = _db_layout(bias, weight, x, h)
-        db = torch.empty(db_shape, dtype=db_dtype, device=x.device)
+        db = db_out if db_out is not None else torch.empty(db_shape, dtype=db_dtype, device=x.device)
     dresidual = None
     if dresidual_out is not None or (
         has_residual and dresidual_dtype is not None and dresidual_dtype != dx.dtype
@@ -261,6 +265,42 @@ def rmsnorm_bwd(
         return _host.fallback_bwd(x, weight, dout, rstd, dresidual_out, has_bias, has_residual, bias)
     dx, dw, db, dresidual = _bwd_cuda(x, weight, dout, rstd, dresidual_out, has_bias, has_residual, bias, h)
     return dx, dw, db, dresidual
+
+
+def _grad_layout(x: Tensor, weight: Optional[Tensor], bias: Optional[Tensor], has_bias: bool):
+    """Shapes of dweight and dbias (None when absent), as rmsnorm_bwd returns them."""
+    h = _head_count(weight, bias, x.shape)
+    dw_shape = weight.shape if weight is not None else None
+    db_shape = _db_layout(bias, weight, x, h)[1] if has_bias else None
+    return dw_shape, db_shape
+
+
+def _rmsnorm_bwd_fp32_grads(x, weight, dout, rstd, dresidual_out, has_bias, has_residual, bias, dw32, db32):
+    """rmsnorm_bwd, except that dweight / dbias are written in fp32 into dw32 / db32
+    (fp32 tensors of the shapes _grad_layout gives) whatever the affine dtypes. A
+    row-sharded backward sums these per-rank fp32 values across ranks and rounds once to
+    the parameters' dtypes. Returns (dx, dresidual)."""
+    if x.dtype not in _SUPPORTED_DTYPES:
+        raise AssertionError("Unsupported dtype")
+    _check_tensor_dtype("Weight", weight)
+    _check_tensor_dtype("Bias", bias)
+    _check_tensor_dtype("dout", dout)
+    _check_tensor_dtype("dresidual_out", dresidual_out)
+    h = _validate_bwd_shapes(x, weight, bias, dout, rstd, dresidual_out)
+    for t in (dw32, db32):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or t.device != x.device):
+            raise ValueError("gradient buffers must be contiguous float32 tensors on x's device")
+    if not x.is_cuda:
+        dx, _, _, dres = _host.fallback_bwd(x, weight, dout, rstd, dresidual_out, False, has_residual, bias)
+        g = dout.float()
+        if dw32 is not None:
+            dw32.copy_(_host.sum_to_affine_shape(g * (x.float() * rstd.float().unsqueeze(-1)), dw32.shape))
+        if db32 is not None:
+            db32.copy_(_host.sum_to_affine_shape(g, db32.shape))
+        return dx, dres
+    dx, _, _, dres = _bwd_cuda(x, weight, dout, rstd, dresidual_out, has_bias, has_residual, bias, h,
+                               dw_out=dw32, db_out=db32)
+    return dx, dres
 
 
 # ---------------------------------------------------------------------------------------

@@ -614,3 +614,64 @@ def test_row_pipelining_on_and_off(monkeypatch, pipe, rows, n):
     dx_err, dw_err = bwd_check(x, w, dy, rstd, dx, dw, 1.6e-2, chunk=512)
     assert dx_err <= 1.0 and dw_err <= 1.0, (dx_err, dw_err, _lib.last_plan())
     assert _lib.device_status(DEV) == (0, 0)
+
+
+@pytest.mark.parametrize("xmode", [None, "1"])
+@pytest.mark.parametrize("rows,n,dtype", [(64, 65536, BF16), (24, 262144, BF16), (20, 262144, F32)])
+def test_split_row_graph_replay_with_new_inputs(monkeypatch, xmode, rows, n, dtype):
+    """Split rows (cfg 3- and cfg 5-shaped: P CTAs per row, by default the global-memory
+    exchange on a cooperative grid) captured once into a CUDA graph and replayed three times
+    with new inputs written in place between replays. Every replay must match the oracle on
+    its own inputs: an exchange record left by the previous replay (same launch parameters)
+    is never taken for this one's. Outputs are NaN-filled before each replay."""
+    if xmode is not None:
+        monkeypatch.setenv("RMSNORM_B200_XMODE", xmode)
+    dev = torch.device(DEV)
+    x = torch.empty((rows, n), dtype=dtype, device=DEV)
+    dy = torch.empty_like(x)
+    w = _g((n,), F32, 300, "weight")
+    out = torch.empty_like(x)
+    rstd = torch.empty(rows, dtype=F32, device=DEV)
+    rstd_in = torch.empty(rows, dtype=F32, device=DEV)
+    dx = torch.empty_like(x)
+    dw = torch.empty(n, dtype=F32, device=DEV)
+    args = _lib.bwd_args(x, dy, rstd_in, w, 1, None, dx, None, dw, None, 1, 1)
+    ws = torch.empty(max(16, _lib.bwd_workspace_bytes(args, dev)), dtype=torch.uint8, device=DEV)
+
+    def step():
+        _lib.fwd(x, None, w, 1, None, 1, out, None, rstd, 1, 1e-6)
+        _lib.bwd(args, dev, ws)
+
+    x.copy_(_g((rows, n), dtype, 301))
+    dy.copy_(_g((rows, n), dtype, 302))
+    step()  # eager warm-up (kernel attributes, plans)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    plan = _lib.last_plan()
+    assert "P=1 " not in plan, plan
+    if xmode == "1":
+        assert "x=global" in plan, plan
+    tol = oracle.y_tolerance(dtype)
+    for rep in range(3):
+        xs = oracle.gen((rows, n), dtype, 310 + rep)
+        dys = oracle.gen((rows, n), dtype, 320 + rep)
+        _, _, o_rstd, y = oracle.fwd(xs, w.cpu())
+        x.copy_(xs.to(DEV))
+        dy.copy_(dys.to(DEV))
+        rstd_in.copy_(o_rstd.to(DEV))
+        for t in (out, dx, dw, rstd):
+            t.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        oracle.check_close(out, y, dtype, f"replay {rep} out [{plan}]", rtol=tol)
+        assert torch.allclose(rstd.cpu(), o_rstd, rtol=1e-5, atol=0), f"replay {rep} rstd"
+        o_dx, o_dw, _, s_dw, _ = oracle.bwd(xs, w.cpu(), dys, o_rstd)
+        oracle.check_close(dx, o_dx, dtype, f"replay {rep} dx", rtol=tol)
+        oracle.check_reduction(dw, o_dw, s_dw, f"replay {rep} dweight")
+    del graph
+    assert _lib.device_status(dev) == (0, 0)
