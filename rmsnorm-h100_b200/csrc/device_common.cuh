@@ -262,6 +262,66 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
   return v;
 }
 
+// ---------------------------------------------------------------------------------------
+// Tensor memory (TMEM) as per-thread accumulator storage. TMEM is 128 lanes x 512 columns
+// of 32-bit cells per SM, normally the tensor cores' accumulator; a streaming kernel has
+// no MMA, so it can keep per-column running sums there instead of in registers. A warp may
+// access only the 32 lanes of its quarter (warp index % 4); with the 32x32b shape, lane i
+// of the warp reads / writes TMEM lane (quarter * 32 + i), `n` consecutive columns.
+// Allocation and deallocation are issued by one whole warp; every tcgen05.ld / st is
+// issued by all 32 lanes of a warp together (the .sync.aligned forms).
+// ---------------------------------------------------------------------------------------
+// Allocates `ncols` columns (a power of two, 32..512) for this CTA and writes the TMEM
+// address to `dst` in shared memory; then gives up the right to allocate again, so other
+// CTAs on the SM are never kept waiting by this one.
+__device__ __forceinline__ void tmem_alloc_warp(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_warp(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Orders this thread's earlier tcgen05 operations before a following thread barrier, and
+// the barrier before this thread's later tcgen05 operations.
+__device__ __forceinline__ void tmem_fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 16 consecutive columns of this lane, as 8 float pairs (element 2i in .x, 2i+1 in .y).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float2 (&v)[8]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float2 (&v)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0].x)), "r"(__float_as_uint(v[0].y)), "r"(__float_as_uint(v[1].x)),
+      "r"(__float_as_uint(v[1].y)), "r"(__float_as_uint(v[2].x)), "r"(__float_as_uint(v[2].y)),
+      "r"(__float_as_uint(v[3].x)), "r"(__float_as_uint(v[3].y)), "r"(__float_as_uint(v[4].x)),
+      "r"(__float_as_uint(v[4].y)), "r"(__float_as_uint(v[5].x)), "r"(__float_as_uint(v[5].y)),
+      "r"(__float_as_uint(v[6].x)), "r"(__float_as_uint(v[6].y)), "r"(__float_as_uint(v[7].x)),
+      "r"(__float_as_uint(v[7].y))
+      : "memory");
+}
+
+// Blocks until this thread's earlier tcgen05.ld (wait_ld) / tcgen05.st (wait_st) are done.
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void named_barrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

@@ -103,15 +103,19 @@ int noalloc_scratch(DeviceState* ds, void** out) {
 
 // Records of the global-memory row-total exchange (split rows on a cooperative grid): a
 // file-scope device array, kXRecSets sets used round-robin by launch, so launches that
-// overlap at their ends (at most a few on one device) use different sets. Each set has
-// one generation counter per CTA group; every execution of a launch draws a fresh
-// generation from it on the device and tags its records with it, so neither an earlier
-// launch nor an earlier replay of the same captured launch can supply a record.
-static __device__ XRecord g_xrec[kXRecSets * kXRecMaxCtas * kXSlots];
-static __device__ uint32_t g_xgen[kXRecSets * kXRecMaxCtas];
+// overlap at their ends (at most a few on one device) use different sets. Within a set,
+// records and generation counters are kept per group size P: the records of a CTA then
+// belong to one CTA group, whose counter gives each of its executions a fresh generation
+// (drawn on the device), so neither another launch nor an earlier replay of the same
+// captured launch can supply a record with the awaited tag.
+static __device__ XRecord g_xrec[kXRecSets * kXGroupSizes * kXRecMaxCtas * kXSlots];
+static __device__ uint32_t g_xgen[kXRecSets * kXGroupSizes * kXRecMaxCtas];
 
-// Next record set (round robin) and its generation counters.
-int next_xset(DeviceState* ds, XRecord** rec, uint32_t** gen) {
+// Next record set (round robin): the records and generation counters of group size P.
+int next_xset(DeviceState* ds, int P, XRecord** rec, uint32_t** gen) {
+  int pidx = 0;
+  while ((2 << pidx) < P) ++pidx;
+  if ((2 << pidx) != P || pidx >= kXGroupSizes) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
   std::lock_guard<std::mutex> lock(ds->mu);
   if (!ds->xrec) {
     void* ptr = nullptr;
@@ -124,9 +128,9 @@ int next_xset(DeviceState* ds, XRecord** rec, uint32_t** gen) {
     ds->xrec = static_cast<XRecord*>(ptr);
     ds->xgen = static_cast<uint32_t*>(gptr);
   }
-  const uint32_t set = ds->xepoch++ % kXRecSets;
-  *rec = ds->xrec + static_cast<size_t>(set) * kXRecMaxCtas * kXSlots;
-  *gen = ds->xgen + static_cast<size_t>(set) * kXRecMaxCtas;
+  const size_t slot = static_cast<size_t>(ds->xepoch++ % kXRecSets) * kXGroupSizes + pidx;
+  *rec = ds->xrec + slot * kXRecMaxCtas * kXSlots;
+  *gen = ds->xgen + slot * kXRecMaxCtas;
   return RMSNORM_B200_OK;
 }
 
@@ -452,8 +456,10 @@ int launch_stream(DeviceState* ds, void (*kernel)(const Params), Params params, 
   if (dry_run) return RMSNORM_B200_OK;
   params.xrec = nullptr;
   params.xgen = nullptr;
-  if (pl.xmode == kXGlobal && next_xset(ds, &params.xrec, &params.xgen) != RMSNORM_B200_OK)
-    return RMSNORM_B200_ERR_CUDA;
+  if (pl.xmode == kXGlobal) {
+    const int st = next_xset(ds, pl.P, &params.xrec, &params.xgen);
+    if (st != RMSNORM_B200_OK) return st;
+  }
   params.pl = pl;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -632,6 +638,32 @@ BwdKernel pick_bwd(int x, int dy, int dx, int dro, int dres, bool db, bool small
   RMSB_BWD(float, F, h16, H, float, F, NoT, NA, NoT, NA)
 #undef RMSB_BWD
 #undef RMSB_BWD_SHAPE
+  return nullptr;
+}
+
+// dbias backwards with the dweight / dbias sums in tensor memory (4 vectors per thread,
+// rows not split, 512-thread CTAs): the same dtype combinations as pick_bwd's large shape.
+BwdKernel pick_bwd_tmem(int x, int dy, int dx, int dro, int dres) {
+#define RMSB_BWD_TM(XT, XC, DT, DC, DXT, DXC, AT, AC, ST, SC)                                         \
+  if (x == XC && dy == DC && dx == DXC && dro == AC && dres == SC)                                   \
+    return bwd_stream_kernel<XT, DT, DXT, AT, ST, true, kMaxVecs, kBlockLarge, 1, false, kMaxVecs, true>;
+  RMSB_BWD_TM(b16, B, b16, B, b16, B, NoT, NA, NoT, NA)
+  RMSB_BWD_TM(h16, H, h16, H, h16, H, NoT, NA, NoT, NA)
+  RMSB_BWD_TM(float, F, float, F, float, F, NoT, NA, NoT, NA)
+  RMSB_BWD_TM(b16, B, b16, B, b16, B, b16, B, b16, B)
+  RMSB_BWD_TM(h16, H, h16, H, h16, H, h16, H, h16, H)
+  RMSB_BWD_TM(float, F, float, F, float, F, float, F, float, F)
+  RMSB_BWD_TM(float, F, b16, B, b16, B, NoT, NA, NoT, NA)
+  RMSB_BWD_TM(float, F, h16, H, h16, H, NoT, NA, NoT, NA)
+  RMSB_BWD_TM(float, F, b16, B, b16, B, float, F, b16, B)
+  RMSB_BWD_TM(float, F, h16, H, h16, H, float, F, h16, H)
+  RMSB_BWD_TM(float, F, b16, B, b16, B, NoT, NA, float, F)
+  RMSB_BWD_TM(float, F, h16, H, h16, H, NoT, NA, float, F)
+  RMSB_BWD_TM(float, F, b16, B, b16, B, float, F, float, F)
+  RMSB_BWD_TM(float, F, h16, H, h16, H, float, F, float, F)
+  RMSB_BWD_TM(float, F, b16, B, float, F, NoT, NA, NoT, NA)
+  RMSB_BWD_TM(float, F, h16, H, float, F, NoT, NA, NoT, NA)
+#undef RMSB_BWD_TM
   return nullptr;
 }
 
@@ -843,19 +875,22 @@ struct BwdPlan {
   int64_t chunk_rows = 0;    // generic: super-rows per chunk
   int64_t W = 0;
   bool need_dw = false, need_db = false;
+  bool tmem = false;         // the dweight / dbias sums of the streaming kernel live in TMEM
   std::string why;
 };
 
 // Tries one (block shape, kernel) candidate; on success fills bp and returns true.
 // col_mode: per-head column mode, the kernel picked by the plan's column count.
+// max_vecs: vectors per thread of the kernel (0 = the default of its dbias variant).
 bool try_bwd_stream(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdKernel kernel, const BlockCfg& bc,
-                    int force_p, BwdPlan* bp, std::string* why, bool col_mode = false) {
+                    int force_p, BwdPlan* bp, std::string* why, bool col_mode = false, int max_vecs = 0) {
   if (!kernel && !col_mode) return false;
   const int in_bytes[3] = {elem_bytes(a->x_dtype), elem_bytes(a->dout_dtype),
                            a->dresidual_out ? elem_bytes(a->dresidual_out_dtype) : 0};
   StreamPlan pl;
-  if (!make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, true,
-                        col_mode ? kMaxVecs : bwd_max_vecs(bp->need_db), bc, force_p, &pl, why, false, col_mode))
+  if (max_vecs == 0) max_vecs = col_mode ? kMaxVecs : bwd_max_vecs(bp->need_db);
+  if (!make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, true, max_vecs, bc, force_p, &pl, why, false,
+                        col_mode))
     return false;
   if (col_mode) {
     // column mode needs whole sweeps of kMaxVecs / cols rows per tile; where only one such
@@ -908,6 +943,20 @@ int plan_bwd(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdPlan* bp) {
       BwdPlan cand = *bp;
       std::string why_c;
       if (try_bwd_stream(ds, a, nullptr, kLarge, 0, &cand, &why_c, true)) { *bp = cand; return RMSNORM_B200_OK; }
+    }
+    // dbias backwards: the 4-vector kernel with its sums in TMEM when a row fits one CTA in
+    // row mode (up to 16384 columns with 512 threads); the 2-vector register kernel otherwise
+    if (bp->need_db && shape != 2 && env_int("RMSNORM_B200_TMEM_ACC", 1)) {
+      if (BwdKernel tk = pick_bwd_tmem(a->x_dtype, a->dout_dtype, a->dx_dtype, dro, dres)) {
+        BwdPlan cand = *bp;
+        std::string why_t;
+        if (try_bwd_stream(ds, a, tk, kLarge, force_p, &cand, &why_t, false, kMaxVecs) && cand.pl.P == 1 &&
+            !cand.pl.seg_mode) {
+          cand.tmem = true;
+          *bp = cand;
+          return RMSNORM_B200_OK;
+        }
+      }
     }
     if (!large && !small) why = "dtype combination";
     // A row split across a cluster waits once per row for its peers. With two CTAs of
@@ -968,6 +1017,7 @@ int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream
       StreamPlan pl = bp.pl;
       st = launch_stream(ds, bp.kernel, p, pl, stream, "bwd_stream", false, nullptr);
       if (st) return st;
+      if (bp.tmem) t_last_plan += " acc=tmem";
     } else {
       GenBwdParams g = {};
       g.rows = a->rows; g.N = a->hidden; g.H = a->heads;

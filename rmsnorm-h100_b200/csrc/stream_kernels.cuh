@@ -60,7 +60,7 @@ extern __shared__ __align__(128) unsigned char rmsb_dyn_smem[];
 // (after full, xbar, xpart, red, done, gbar and gpart).
 constexpr uint32_t kXTagOff = kMaxStages * 8 + kXSlots * 8 + kXSlots * kMaxCluster * 4 + 64 * 4 + kMaxStages * 4 +
                               16 * kGroupRed * 8 + kGroupRed * 16 * 4;
-static_assert(kXTagOff + 4 <= kSmemReserve, "barrier area exceeds its reserve");
+static_assert(kXTagOff + 8 <= kSmemReserve, "barrier area exceeds its reserve");
 
 struct SmemLayout {
   uint64_t* full;   // [kMaxStages] slot filled
@@ -71,6 +71,7 @@ struct SmemLayout {
   uint64_t* gbar;   // [16 groups][kGroupRed] split-phase row-group reductions (LayerNorm)
   float* gpart;     // [kGroupRed][16 warps] their per-warp partials
   uint32_t* xgen;   // [1] the execution generation of the global-memory exchange
+  uint32_t* tmem;   // [1] TMEM address of the backward's accumulators (kTmemAcc kernels)
 };
 
 __device__ __forceinline__ SmemLayout carve_smem(unsigned char* smem, const StreamPlan& pl) {
@@ -84,6 +85,7 @@ __device__ __forceinline__ SmemLayout carve_smem(unsigned char* smem, const Stre
   L.gbar = reinterpret_cast<uint64_t*>(L.done + kMaxStages);
   L.gpart = reinterpret_cast<float*>(L.gbar + 16 * kGroupRed);
   L.xgen = reinterpret_cast<uint32_t*>(tail + kXTagOff);
+  L.tmem = L.xgen + 1;
   return L;
 }
 
@@ -198,17 +200,17 @@ __device__ __forceinline__ uint32_t xrec_tag(const StreamPlan& pl, uint32_t seq)
 }
 
 // Draws this execution's generation for CTA group `cid` (kXGlobal; every thread of the
-// CTA calls it, after pdl_wait). Each of the group's P CTAs adds kMaxCluster / P to the
-// group's counter, so every execution adds exactly kMaxCluster whatever its P, and the P
-// CTAs of one execution all read old values in [g * kMaxCluster, (g + 1) * kMaxCluster):
-// the same generation g, with no wait among them. This holds as long as two executions
-// that share a record set and a group do not run at the same time on the GPU (launches of
-// one stream never do; the host hands consecutive launches different record sets).
-// The tag base is kept in shared memory (not in a register for the whole kernel).
+// CTA calls it, after pdl_wait). The group's counter (one per group of this P) gets one
+// increment from each of its P CTAs per execution, so the P CTAs of one execution all read
+// old values in [g * P, (g + 1) * P): the same generation g, with no wait among them. This
+// holds as long as two executions that share a record set and a group do not run at the
+// same time on the GPU (launches of one stream never do; the host hands consecutive
+// launches different record sets). The tag base is kept in shared memory, not in a
+// register for the whole kernel.
 __device__ __forceinline__ void xgen_begin(const StreamPlan& pl, const SmemLayout& L, uint32_t* xgen, int64_t cid) {
   if (pl.P <= 1 || pl.xmode != kXGlobal) return;
   if (threadIdx.x == 0) {
-    const uint32_t g = atomicAdd(xgen + cid, static_cast<uint32_t>(kMaxCluster / pl.P)) / kMaxCluster;
+    const uint32_t g = atomicAdd(xgen + cid, 1u) / static_cast<uint32_t>(pl.P);
     *L.xgen = 0x80000000u | ((g & 0x3fffffffu) << 1);
   }
   __syncthreads();
@@ -1012,11 +1014,22 @@ __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& 
 // X: saved input dtype; DY: dout dtype; DXT: dx dtype; DROT: dresidual_out dtype (NoT =
 // none); DREST: dresidual dtype (NoT = not written); kRstdBulk: see bwd_issue; kCols <
 // kVecs: per-head column mode, as in the forward (the thread's weight and dweight / dbias
-// accumulators cover kCols columns).
+// accumulators cover kCols columns). kTmemAcc: the dweight / dbias accumulators live in
+// tensor memory instead of registers (16 columns of the thread's TMEM lane per vector:
+// dweight pairs, then dbias pairs). Weight, dweight and dbias of 4 vectors per thread
+// need 96 registers, more than 128-register threads can spare beside the passes' working
+// set; with the sums in TMEM a dbias backward keeps 4 vectors per thread, so a 16384-wide
+// row fits one CTA instead of a 2-CTA cluster. Planned for unsplit rows in row mode only
+// (thread groups of whole warps, so every warp issues its TMEM accesses together); the
+// split-row loop is compiled out of these kernels.
 template <typename X, typename DY, typename DXT, typename DROT, typename DREST, bool kHasDb, int kVecs,
-          int kBlock, int kMinBlocks, bool kRstdBulk = false, int kCols = kVecs>
+          int kBlock, int kMinBlocks, bool kRstdBulk = false, int kCols = kVecs, bool kTmemAcc = false>
 __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const BwdParams p) {
   static_assert(kVecs % kCols == 0, "column mode: whole rows per thread");
+  static_assert(!kTmemAcc || (kHasDb && kCols == kVecs && kVecs == 4), "TMEM accumulators: 4-vector dbias rows");
+  // TMEM columns of the CTA: 64 per warp (4 vectors x 16), the warps of a lane quarter
+  // side by side
+  constexpr uint32_t kTmemCols = static_cast<uint32_t>(kBlock / 128) * 64u;
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr bool kDro = Present<DROT>::value;
   constexpr bool kDres = Present<DREST>::value;
@@ -1043,7 +1056,23 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   }
   // row mode with one row per group per tile: rows pipelined one tile deep (when planned)
   const bool rows_pipe = pl.pipe_rows && !pl.seg_mode && pl.P == 1 && pl.R == pl.rps && pl.S >= 3;
+  if constexpr (kTmemAcc) {
+    if (warp == 0) tmem_alloc_warp(L.tmem, kTmemCols);
+    tmem_fence_before_sync();
+  }
   init_barriers(L, pl, rows_pipe);
+  // this thread's accumulators: TMEM lane 32 * (warp % 4) + lane, 64 columns per warp
+  uint32_t tacc = 0;
+  if constexpr (kTmemAcc) {
+    tmem_fence_after_sync();
+    tacc = *L.tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + static_cast<uint32_t>(warp >> 2) * 64u;
+    float2 z[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) z[i] = splat2(0.f);
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) tmem_st16(tacc + 16u * k, z);
+    tmem_wait_st();
+  }
   pdl_wait();  // every global access of the launch follows this point
   pdl_launch_dependents();
   xgen_begin(pl, L, p.xgen, cid);
@@ -1081,17 +1110,23 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     if (in_group && gl + (k % kCols) * G < pl.vslice) vmask |= 1u << k;
 
   // weight of the thread's columns and its dweight / dbias accumulators, as float pairs
+  // (the accumulators are in TMEM instead for kTmemAcc)
+  constexpr int kAcc = kTmemAcc ? 1 : kCols;
   float2 wr[kCols][4];
-  float2 dw[kCols][4];
-  float2 db[kHasDb ? kCols : 1][4];
+  float2 dw[kAcc][4];
+  float2 db[(kHasDb && !kTmemAcc) ? kCols : 1][4];
 #pragma unroll
   for (int k = 0; k < kCols; ++k) {
     const int64_t c = slice_elt0 + static_cast<int64_t>(gl + k * G) * 8;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) { wr[k][i] = splat2(1.f); dw[k][i] = splat2(0.f); }
-    if constexpr (kHasDb) {
+    for (int i = 0; i < 4; ++i) wr[k][i] = splat2(1.f);
+    if constexpr (!kTmemAcc) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) db[kHasDb ? k : 0][i] = splat2(0.f);
+      for (int i = 0; i < 4; ++i) dw[k % kAcc][i] = splat2(0.f);
+      if constexpr (kHasDb) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) db[kHasDb ? k : 0][i] = splat2(0.f);
+      }
     }
     if (((vmask >> k) & 1u) && p.w != nullptr) load8p_rt(p.w, p.w_dt, p.w_per_head ? c : c % pl.N, wr[k]);
   }
@@ -1109,10 +1144,40 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     for (int i = 0; i < 4; ++i) {
       const float2 t = mul2(xv[i], dv[i]);
       acc = fma2(t, wr[k % kCols][i], acc);
-      dw[k % kCols][i] = fma2(t, r2, dw[k % kCols][i]);
-      if constexpr (kHasDb) db[kHasDb ? k % kCols : 0][i] = add2(db[kHasDb ? k % kCols : 0][i], dv[i]);
+      if constexpr (!kTmemAcc) {
+        dw[k % kAcc][i] = fma2(t, r2, dw[k % kAcc][i]);
+        if constexpr (kHasDb) db[kHasDb ? k % kCols : 0][i] = add2(db[kHasDb ? k % kCols : 0][i], dv[i]);
+      }
     }
     return (acc.x + acc.y) * r;
+  };
+  // the same with the vector's dweight / dbias sums held in TMEM: `valid` false (a vector
+  // outside the slice) still loads and stores them, since every lane of the warp issues
+  // the TMEM accesses together
+  auto dot_acc_tmem = [&](const X* xp, const DY* dp, float r, int k, bool valid) {
+    float2 a[8];  // dweight pairs 0..3, dbias pairs 4..7
+    tmem_ld16(tacc + 16u * k, a);
+    float d = 0.f;
+    float2 xv[4], dv[4];
+    if (valid) {
+      Pair8<X>::load(xp, xv);
+      Pair8<DY>::load(dp, dv);
+    }
+    tmem_wait_ld();
+    if (valid) {
+      const float2 r2 = splat2(r);
+      float2 acc = splat2(0.f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 t = mul2(xv[i], dv[i]);
+        acc = fma2(t, wr[k % kCols][i], acc);
+        a[i] = fma2(t, r2, a[i]);
+        a[4 + i] = add2(a[4 + i], dv[i]);
+      }
+      d = (acc.x + acc.y) * r;
+    }
+    tmem_st16(tacc + 16u * k, a);
+    return d;
   };
   // pass 2 of thread vector k: dx = r * dy * w - r^2 c x (+ dresidual_out), stored to dx
   // and dresidual
@@ -1151,6 +1216,16 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   };
   // pass 1: partial dot products per vector, dweight / dbias accumulation
   auto pass1 = [&](const RowPtrs& rp, float (&part)[kVecs], float (&rstd_k)[kVecs]) {
+    if constexpr (kTmemAcc) {
+      tmem_wait_st();  // the previous row's sums are in TMEM before they are read again
+      const float r = rp.rstd[0];  // row mode: one rstd per row
+#pragma unroll
+      for (int k = 0; k < kVecs; ++k) {
+        rstd_k[k] = r;
+        part[k] = dot_acc_tmem(rp.x + k * G8, rp.dy + k * G8, r, k, (vmask >> k) & 1u);
+      }
+      return;
+    }
 #pragma unroll
     for (int k = 0; k < kVecs; ++k) {
       part[k] = 0.f;
@@ -1345,7 +1420,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
         issue_unit(q + S, s);
       if (++s == S) { s = 0; ph ^= 1u; }
     }
-  } else if (active_warp) {
+  } else if (active_warp && !kTmemAcc) {  // (TMEM-accumulator kernels are planned for P == 1 only)
     // --------- split-row loop (rows split over the cluster, one row per tile) ---------
     const int lag = pl.lag;
     int s1 = 0, s2 = 0;
@@ -1408,12 +1483,32 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   // one partial row per (cluster, row group): the groups of a CTA own the same columns.
   // Every owned column is written, zeros included, so the reduction reads no stale data.
   const int64_t pbase = (cid * pl.rps + gid) * pl.W + slice_elt0 + gl * 8;
+  if constexpr (kTmemAcc) {
+    tmem_wait_st();
 #pragma unroll
-  for (int k = 0; k < kCols; ++k) {
-    if ((vmask >> k) & 1u) {
-      if (p.dw_part != nullptr) Pair8<float>::store(p.dw_part + pbase + k * G8, dw[k]);
-      if constexpr (kHasDb) {
-        if (p.db_part != nullptr) Pair8<float>::store(p.db_part + pbase + k * G8, db[kHasDb ? k : 0]);
+    for (int k = 0; k < kVecs; ++k) {
+      float2 a[8];
+      tmem_ld16(tacc + 16u * k, a);
+      tmem_wait_ld();
+      if ((vmask >> k) & 1u) {
+        if (p.dw_part != nullptr) Pair8<float>::store(p.dw_part + pbase + k * G8, *reinterpret_cast<float2(*)[4]>(a));
+        if (p.db_part != nullptr)
+          Pair8<float>::store(p.db_part + pbase + k * G8, *reinterpret_cast<float2(*)[4]>(a + 4));
+      }
+    }
+    // every warp's TMEM accesses are done before warp 0 frees the columns
+    tmem_fence_before_sync();
+    __syncthreads();
+    tmem_fence_after_sync();
+    if (warp == 0) tmem_dealloc_warp(*L.tmem, kTmemCols);
+  } else {
+#pragma unroll
+    for (int k = 0; k < kCols; ++k) {
+      if ((vmask >> k) & 1u) {
+        if (p.dw_part != nullptr) Pair8<float>::store(p.dw_part + pbase + k * G8, dw[k % kAcc]);
+        if constexpr (kHasDb) {
+          if (p.db_part != nullptr) Pair8<float>::store(p.db_part + pbase + k * G8, db[kHasDb ? k : 0]);
+        }
       }
     }
   }

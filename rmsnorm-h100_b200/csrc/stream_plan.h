@@ -65,14 +65,18 @@ constexpr int kXGlobal = 1;
 
 // One row total of one CTA in the global-memory exchange, in one 64-bit word written and
 // read whole (single-copy atomic): high half = tag, low half = the float's bits. Tag =
-// 0x80000000 | (execution generation << 1) | (bit 0 of row / kXSlots). The generation is
-// drawn on the device by every execution of the launch (a graph replay of the same launch
-// parameters draws a new one), so a reader waiting for a row finds that row's word, the
-// one of the row kXSlots before it, or a word of an earlier execution (another
-// generation); never-written records (zero) carry no valid tag.
+// 0x80000000 | (execution generation << 1) | (bit 0 of row / kXSlots). Records are kept
+// per record set and per group size P, so the records of CTA c belong to one CTA group
+// (CTAs c - c % P .. c - c % P + P - 1) and only that group's executions write them; the
+// group's generation counter gives every execution a generation of its own, drawn on the
+// device (a graph replay of the same launch parameters draws a new one). A reader waiting
+// for a row therefore finds that row's word, the one of the row kXSlots before it, or a
+// word of an earlier execution of the same group (a smaller generation, modulo 2^30);
+// never-written records (zero) carry no valid tag.
 using XRecord = unsigned long long;
 constexpr int kXRecSets = 4;        // record sets, used round-robin by launch epoch
 constexpr int kXRecMaxCtas = 512;   // CTAs of a global-exchange grid
+constexpr int kXGroupSizes = 4;     // P = 2, 4, 8, 16 (index log2(P) - 1)
 
 struct FwdParams {
   StreamPlan pl;
@@ -87,8 +91,8 @@ struct FwdParams {
   int32_t w_per_head, b_per_head;  // 1 when the affine tensor is [H, N]
   float eps;
   float* mean;     // LayerNorm: per-row mean (null = not stored)
-  XRecord* xrec;   // kXGlobal: this launch's record set ([kXRecMaxCtas][kXSlots])
-  uint32_t* xgen;  // kXGlobal: the set's generation counters, one per CTA group
+  XRecord* xrec;   // kXGlobal: this launch's records for its P ([kXRecMaxCtas][kXSlots])
+  uint32_t* xgen;  // kXGlobal: the generation counters of its P, one per CTA group
 };
 
 struct BwdParams {

@@ -17,7 +17,11 @@ from typing import Optional, Tuple
 import torch
 from torch import Tensor
 
-from . import rmsnorm as _api
+# The submodule, not the package attribute `rmsnorm` (the package re-exports the function
+# of that name, which shadows the submodule).
+import importlib
+
+_api = importlib.import_module(__package__ + ".rmsnorm")
 
 _EMPTY = (0,)
 

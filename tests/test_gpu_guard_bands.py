@@ -108,9 +108,13 @@ BWD_CASES = [
     (9, 24, F16, F16, False, True, 1, None, "mode=seg"),
     (37 * 32, 128, F16, F16, False, True, 32, None, "cols=1"),
     (3, 262144, BF16, BF16, False, False, 1, None, "bwd_stream"),
-    (4, 262144, F32, F32, False, True, 1, None, "bwd_stream"),
-    (70, 65536, BF16, BF16, False, True, 1, {"RMSNORM_B200_XMODE": "1", "RMSNORM_B200_FORCE_CLUSTER": "4"},
+    (4, 262144, F32, F32, False, False, 1, None, "bwd_stream"),
+    (4, 262144, F32, F32, False, True, 1, None, "bwd_generic"),  # dbias rows wider than 16 CTAs hold
+    (70, 65536, BF16, BF16, False, True, 1, {"RMSNORM_B200_XMODE": "1", "RMSNORM_B200_FORCE_CLUSTER": "8"},
      "x=global"),
+    (37, 16384, F32, BF16, False, True, 1, None, "acc=tmem"),  # dweight / dbias sums in TMEM
+    (301, 12288, BF16, BF16, True, True, 1, None, "acc=tmem"),  # last vector of the slice ragged
+    (37, 16384, F32, BF16, False, True, 1, {"RMSNORM_B200_TMEM_ACC": "0"}, "P=2"),
     (6, 100, BF16, BF16, True, True, 1, None, "bwd_generic"),
 ]
 

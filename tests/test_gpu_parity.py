@@ -675,3 +675,17 @@ def test_split_row_graph_replay_with_new_inputs(monkeypatch, xmode, rows, n, dty
         oracle.check_reduction(dw, o_dw, s_dw, f"replay {rep} dweight")
     del graph
     assert _lib.device_status(dev) == (0, 0)
+
+
+@pytest.mark.parametrize("M,N,dtype,dro", [(7, 16384, F32, False), (300, 4096, BF16, True), (33, 12288, F16, False),
+                                          (2000, 1024, F16, False), (1, 16384, BF16, True)])
+def test_bwd_dbias_sums_in_tmem(monkeypatch, M, N, dtype, dro):
+    """dbias backwards whose rows fit one CTA keep the dweight / dbias sums in tensor memory
+    (4 vectors per thread, no cluster split): results match the oracle and repeat bitwise;
+    the register-accumulator kernel (TMEM off) matches the oracle as well."""
+    plan = _bwd_case(M, N, dtype, has_bias=True, dro=dro, seed=400 + M, expect="acc=tmem")
+    assert "P=1 " in plan, plan
+    monkeypatch.setenv("RMSNORM_B200_TMEM_ACC", "0")
+    plan = _bwd_case(M, N, dtype, has_bias=True, dro=dro, seed=400 + M)
+    assert "acc=tmem" not in plan, plan
+    assert _lib.device_status(DEV) == (0, 0)
