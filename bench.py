@@ -199,6 +199,7 @@ class Runner:
         from rmsnorm import _lib
 
         self.w, self.t, self.dev, self.group, self.lib = w, t, dev, group, _lib
+        self.peer = None  # native peer group handle (set when the fused all-reduce is used)
         self.h = h = w.get("heads", 1)
         x = t["x"]
         rows = x.shape[0]
@@ -234,8 +235,10 @@ class Runner:
         else:
             self.lib.fwd(t["x"], t.get("res"), t["w"], h, t["b"], h, self.out, self.ro, self.rstd, h, EPS)
 
-    def bwd(self):
-        self.lib.bwd(self.args, self.dev, self.ws)
+    def bwd(self, local=False):
+        """The backward; with a peer group (and not `local`) its dweight / dbias are summed
+        over the ranks by the library's fused reduction + all-reduce kernel."""
+        self.lib.bwd(self.args, self.dev, self.ws, peer_group=None if local else self.peer)
 
     def allreduce(self, buf=None):
         import torch.distributed as dist
@@ -248,7 +251,7 @@ class Runner:
             self.fwd()
         if kind in ("bwd", "train"):
             self.bwd()
-            if self.group is not None:
+            if self.group is not None and self.peer is None:
                 self.allreduce()
 
 
@@ -764,6 +767,9 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2fb")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="strong: the workload's rows are split across the ranks; weak: every rank runs them all")
+    ap.add_argument("--allreduce", choices=["auto", "peer", "nccl"], default="auto",
+                    help="dweight/dbias across ranks: the library's fused kernel over peer memory (peer), NCCL, "
+                         "or peer unless its set-up fails (auto)")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-directions", action="store_true", help="skip the per-direction timings")
@@ -823,6 +829,33 @@ def main():
     sets = [make_inputs(w, rows, dev, 100 * i + 7 * rank) for i in range(pool)]
     runners = [Runner(w, t, dev, group) for t in sets]
 
+    # dweight / dbias across ranks: the library's fused reduction + all-reduce over peer
+    # memory, or NCCL (auto: the fused kernel unless its set-up fails on any rank)
+    peer_group, ar_backend = None, "nccl" if group is not None else None
+    if group is not None and kind in ("bwd", "train") and args.allreduce != "nccl":
+        import torch.distributed as dist
+
+        from rmsnorm.distributed import PeerGroup
+
+        ok = 1
+        try:
+            peer_group = PeerGroup(runners[0].grads.numel(), group=group)
+        except Exception as exc:  # e.g. no CUDA IPC between the ranks' GPUs
+            log(f"[bench] peer group set-up failed on rank {rank}: {exc}")
+            ok = 0
+        flag = torch.tensor([ok], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+        if flag.item() == 1:
+            ar_backend = "peer"
+            for r in runners:
+                r.peer = peer_group.handle
+        else:
+            if peer_group is not None:
+                peer_group.close()
+            peer_group = None
+            if args.allreduce == "peer":
+                raise SystemExit("--allreduce peer: the peer group could not be set up")
+
     for i in range(args.warmup):
         runners[i % pool].step()
     torch.cuda.synchronize(dev)
@@ -860,7 +893,7 @@ def main():
                                  "bytes_per_rank": fb, "gbs_per_gpu": round(fb / (fwd_ms * 1e-3) / 1e9, 1),
                                  "frac": round(fb / (fwd_ms * 1e-3) / 1e9 / peak, 4), "plan": plans.get("fwd")}
             kern_ms = fwd_ms
-        tb = Timed(lambda i: runners[i % pool].bwd(), args.steps, dev, use_graph)
+        tb = Timed(lambda i: runners[i % pool].bwd(local=True), args.steps, dev, use_graph)
         bwd_ms = tb.run(group)[0] / args.steps
         tb.release()
         bb = bwd_bytes(w, rows, x_size=esize(w["ro"]) if kind == "train" else None)
@@ -868,12 +901,26 @@ def main():
                              "bytes_per_rank": bb, "gbs_per_gpu": round(bb / (bwd_ms * 1e-3) / 1e9, 1),
                              "frac": round(bb / (bwd_ms * 1e-3) / 1e9 / peak, 4), "plan": plans.get("bwd")}
         if group is not None:
+            ar = {"bytes": runners[0].grads.numel() * 4, "backend": ar_backend}
+            if peer_group is not None:
+                # the fused kernel replaces reduce_partials_kernel: its cost is the backward
+                # with it minus the backward with the local reduction
+                tp = Timed(lambda i: runners[i % pool].bwd(), args.steps, dev, use_graph)
+                bwd_peer_ms = tp.run(group)[0] / args.steps
+                tp.release()
+                ar["bwd_with_fused_allreduce_ms"] = round(bwd_peer_ms, 5)
+                ar["us"] = round((bwd_peer_ms - bwd_ms) * 1e3, 2)
+                ar["kernel"] = "reduce_allreduce_kernel (reduction of the partial rows + all-reduce over peer memory)"
             ta = Timed(lambda i: runners[i % pool].allreduce(runners[i % pool].ar_scratch), args.steps, dev,
                        use_graph)
             ar_ms = ta.run(group)[0] / args.steps
             ta.release()
-            directions["allreduce"] = {"us": round(ar_ms * 1e3, 2), "bytes": runners[0].grads.numel() * 4,
-                                       "backend": "nccl", "timing": ta.how}
+            if peer_group is None:
+                ar["us"] = round(ar_ms * 1e3, 2)
+            else:
+                ar["nccl_allreduce_alone_us"] = round(ar_ms * 1e3, 2)
+            ar["timing"] = ta.how
+            directions["allreduce"] = ar
         if kind == "bwd":
             kern_ms = None
     if kern_ms is None:
@@ -917,6 +964,7 @@ def main():
                 "workload": w["desc"], "workload_name": args.workload, "global_rows": sum(all_rows),
                 "rows_per_rank": rows, "hidden": w["n"], "heads": h,
                 "parallelism": f"dp{world} (row shards, one rank per GPU; {args.scaling} scaling)",
+                "grad_allreduce": ar_backend,
                 "bytes_per_step_all_ranks": job_bytes, "bytes_per_step_rank0": algo_bytes(w, rows),
                 "l2": ("inputs larger than L2" if pool == 1 else f"rotating pool of {pool} input sets > L2"),
                 "path": plans if plans else plan,
@@ -947,6 +995,9 @@ def main():
 
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
+        if peer_group is not None:
+            peer_group.close()
+            dist.barrier(group=group)
         dist.destroy_process_group()
     if line is not None:
         print(json.dumps(line), flush=True)

@@ -155,6 +155,60 @@ int rmsnorm_b200_bwd(const rmsnorm_b200_bwd_args* args, void* workspace, size_t 
 #define RMSNORM_B200_NOALLOC_SCRATCH_BYTES (16u << 20)
 int rmsnorm_b200_bwd_noalloc(const rmsnorm_b200_bwd_args* args, void* stream);
 
+/* ---- Row-sharded backward over the GPUs of one node (one process per GPU) ----
+ * No counterpart in the reference (single-GPU). A row-sharded training step sums every
+ * rank's dweight / dbias; rmsnorm_b200_bwd_allreduce does that sum in the same kernel as
+ * the backward's final fixed-order reduction of the partial rows: each rank pushes its
+ * column sums, tagged, into every rank's exchange buffer over NVLink (peer stores, no
+ * multicast) and sums the ranks' values in rank order, so every rank gets identical bits.
+ *
+ * Set-up, once per group: every rank calls rmsnorm_b200_peer_group_create (allocates and
+ * zeroes its exchange buffer, returns its CUDA IPC handle), the ranks exchange the handles
+ * (e.g. an all-gather over the process group), then every rank calls
+ * rmsnorm_b200_peer_group_connect with all handles in rank order. Every rank must then
+ * make the same sequence of rmsnorm_b200_bwd_allreduce calls with the same gradient shapes.
+ * A rank waits for its peers at most the peer timeout (rmsnorm_b200_set_peer_timeout_ns,
+ * default 10 s); a wait that runs out records RMSNORM_B200_ERR_DEVICE_TIMEOUT in the device
+ * status word and the group must be re-created. */
+#define RMSNORM_B200_IPC_HANDLE_BYTES 64
+#define RMSNORM_B200_MAX_PEERS 8
+typedef struct rmsnorm_b200_peer_group rmsnorm_b200_peer_group;
+
+/* Bytes of the exchange buffer of a rank in a group of `world` ranks whose calls sum at
+ * most `max_grad_floats` gradient values (dweight + dbias elements). */
+int rmsnorm_b200_peer_buffer_size(int32_t world, int64_t max_grad_floats, size_t* bytes);
+
+/* Creates this rank's member of a group on the current device: allocates (cudaMalloc,
+ * set-up only) and zeroes its exchange buffer and writes the buffer's CUDA IPC handle
+ * (RMSNORM_B200_IPC_HANDLE_BYTES bytes) to `ipc_handle`. */
+int rmsnorm_b200_peer_group_create(int32_t rank, int32_t world, int64_t max_grad_floats, void* ipc_handle,
+                                   rmsnorm_b200_peer_group** group);
+
+/* Maps the other ranks' buffers: `ipc_handles` holds world handles in rank order (this
+ * rank's own entry is ignored). */
+int rmsnorm_b200_peer_group_connect(rmsnorm_b200_peer_group* group, const void* ipc_handles);
+
+/* The same with device pointers this device can address for each rank's buffer (world
+ * entries in rank order; this rank's own entry is ignored), for callers that map the
+ * buffers themselves. */
+int rmsnorm_b200_peer_group_connect_buffers(rmsnorm_b200_peer_group* group, void* const* buffers);
+
+/* Device address of this rank's exchange buffer (for rmsnorm_b200_peer_group_connect_buffers
+ * of the other ranks when they share this process's address space). */
+int rmsnorm_b200_peer_group_buffer(rmsnorm_b200_peer_group* group, void** buffer);
+
+/* Unmaps the peers' buffers and frees this rank's buffer. No call may be in flight. */
+int rmsnorm_b200_peer_group_destroy(rmsnorm_b200_peer_group* group);
+
+/* Longest wait for the peers inside rmsnorm_b200_bwd_allreduce (at least 1 ms). */
+int rmsnorm_b200_set_peer_timeout_ns(uint64_t timeout_ns);
+
+/* rmsnorm_b200_bwd on this rank's rows, with dweight / dbias summed over the group's
+ * ranks (identical on every rank). Same arguments and workspace as rmsnorm_b200_bwd; the
+ * group's device must be current. */
+int rmsnorm_b200_bwd_allreduce(const rmsnorm_b200_bwd_args* args, void* workspace, size_t workspace_bytes,
+                               rmsnorm_b200_peer_group* group, void* stream);
+
 /* LayerNorm forward over rows of `hidden` elements: mean, variance as the mean of squared
  * deviations (fp32), out = (x - mean) * rsqrt(var + eps) * weight + bias. Replaces the
  * PyTorch implementation of layernorm_fwd (rmsnorm/rmsnorm.py:655-676); the reference has

@@ -19,7 +19,9 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
 NAME = "rmsnorm_ref_ext"
-DEFAULT_REF = Path(os.environ.get("RMSNORM_REFERENCE_ROOT", "/root/reference"))
+# The reference checkout: RMSNORM_REFERENCE_ROOT, else a directory named `reference` next
+# to this repository's root (the layout of the build container); absent elsewhere.
+DEFAULT_REF = Path(os.environ.get("RMSNORM_REFERENCE_ROOT", str(HERE.parent.parent / "reference")))
 
 
 def built_path() -> Path:

@@ -33,6 +33,7 @@ enum WaitSite : int {
   kSiteBwdCluster = 6,
   kSiteDrain = 7,
   kSiteSelftest = 8,
+  kSitePeer = 9,  // a rank's dweight / dbias sums in the peer all-reduce
 };
 
 __device__ __forceinline__ void record_error(int code, int where) {

@@ -21,7 +21,23 @@
 #include <vector>
 
 #include "generic_kernels.cuh"
+#include "peer_allreduce.cuh"
 #include "stream_kernels.cuh"
+
+// One rank's member of a peer group (opaque in the C ABI): the exchange buffers of the
+// fused dweight / dbias all-reduce (peer_allreduce.cuh).
+struct rmsnorm_b200_peer_group {
+  int rank = 0;
+  int world = 0;
+  int device = -1;
+  int64_t max_floats = 0;                                 // words per (parity, source) slot
+  void* buffer = nullptr;                                 // this rank's exchange buffer (owned)
+  void* opened[RMSNORM_B200_MAX_PEERS] = {};              // IPC mappings of the peers' buffers
+  unsigned long long* recv[RMSNORM_B200_MAX_PEERS] = {};  // each rank's receive area, as this device sees it
+  bool connected = false;
+};
+static_assert(sizeof(cudaIpcMemHandle_t) == RMSNORM_B200_IPC_HANDLE_BYTES, "IPC handle size");
+static_assert(RMSNORM_B200_MAX_PEERS == rmsb200::kMaxPeers, "peer count");
 
 namespace rmsb200 {
 namespace {
@@ -993,9 +1009,27 @@ size_t workspace_for(const BwdPlan& bp) {
   return (bp.need_dw ? per : 0) + (bp.need_db ? per : 0);
 }
 
-int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream_t stream) {
+// Gradient values (dweight + dbias elements) a backward with these arguments produces.
+int64_t grad_floats(const rmsnorm_b200_bwd_args* a) {
+  const int64_t W = a->hidden * a->heads;
+  int64_t n = 0;
+  if (a->dweight) n += (a->weight_heads == 1 && a->heads > 1) ? a->hidden : W;
+  if (a->dbias) n += (a->dbias_heads == 1 && a->heads > 1) ? a->hidden : W;
+  return n;
+}
+
+// group: when not null, the dweight / dbias sums are all-reduced over the group's ranks by
+// the fused reduction kernel instead of reduce_partials_kernel.
+int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream_t stream,
+           rmsnorm_b200_peer_group* group = nullptr) {
   int st = check_bwd(a);
   if (st) return st;
+  if (group != nullptr) {  // checked before anything is launched: the ranks stay in step
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != group->device || !group->connected)
+      return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+    if (grad_floats(a) > group->max_floats) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  }
   DeviceState* ds = nullptr;
   st = get_device_state(&ds);
   if (st) return st;
@@ -1062,7 +1096,18 @@ int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream
   };
   if (a->dweight) add_job(dw_part, a->dweight, a->dweight_dtype, a->weight_heads);
   if (a->dbias) add_job(db_part, a->dbias, a->dbias_dtype, a->dbias_heads);
-  if (njobs > 0) {
+  if (njobs > 0 && group != nullptr) {
+    PeerParams pp = {};
+    for (int q = 0; q < group->world; ++q) pp.recv[q] = group->recv[q];
+    pp.seq = static_cast<uint32_t*>(group->buffer);
+    pp.rank = group->rank;
+    pp.world = group->world;
+    pp.stride = group->max_floats;
+    reduce_allreduce_kernel<<<kARBlocks, kARThreads, 0, stream>>>(rp, pp);
+    if (cudaGetLastError() != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    t_last_plan += " allreduce=peer world=" + std::to_string(group->world);
+  } else if (njobs > 0) {
     const dim3 grid(static_cast<unsigned>((max_wout + kReduceCols - 1) / kReduceCols), static_cast<unsigned>(njobs));
     reduce_partials_kernel<<<grid, kReduceThreads, 0, stream>>>(rp);
     if (cudaGetLastError() != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
@@ -1105,6 +1150,107 @@ extern "C" int rmsnorm_b200_bwd_workspace_size(const rmsnorm_b200_bwd_args* args
 extern "C" int rmsnorm_b200_bwd(const rmsnorm_b200_bwd_args* args, void* workspace,
                                 size_t workspace_bytes, void* stream) {
   return do_bwd(args, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int rmsnorm_b200_peer_buffer_size(int32_t world, int64_t max_grad_floats, size_t* bytes) {
+  if (!bytes || world < 1 || world > RMSNORM_B200_MAX_PEERS || max_grad_floats < 1)
+    return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  *bytes = static_cast<size_t>(kPeerBufferHeader) + 2ull * static_cast<size_t>(world) *
+                                                        static_cast<size_t>(max_grad_floats) * 8ull;
+  return RMSNORM_B200_OK;
+}
+
+extern "C" int rmsnorm_b200_peer_group_create(int32_t rank, int32_t world, int64_t max_grad_floats,
+                                              void* ipc_handle, rmsnorm_b200_peer_group** group) {
+  if (!group || !ipc_handle || rank < 0 || rank >= world) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  *group = nullptr;
+  size_t bytes = 0;
+  int st = rmsnorm_b200_peer_buffer_size(world, max_grad_floats, &bytes);
+  if (st) return st;
+  auto g = std::make_unique<rmsnorm_b200_peer_group>();
+  if (cudaGetDevice(&g->device) != cudaSuccess) return RMSNORM_B200_ERR_NO_DEVICE;
+  g->rank = rank;
+  g->world = world;
+  g->max_floats = max_grad_floats;
+  if (cudaMalloc(&g->buffer, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return RMSNORM_B200_ERR_CUDA;
+  }
+  cudaIpcMemHandle_t h;
+  // zeroed before any peer can reach it: the handle leaves this call only afterwards
+  if (cudaMemset(g->buffer, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&h, g->buffer) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(g->buffer);
+    return RMSNORM_B200_ERR_CUDA;
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  g->recv[rank] = reinterpret_cast<unsigned long long*>(static_cast<char*>(g->buffer) + kPeerBufferHeader);
+  *group = g.release();
+  return RMSNORM_B200_OK;
+}
+
+extern "C" int rmsnorm_b200_peer_group_connect(rmsnorm_b200_peer_group* g, const void* ipc_handles) {
+  if (!g || !ipc_handles || g->connected) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != g->device) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  for (int q = 0; q < g->world; ++q) {
+    if (q == g->rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const char*>(ipc_handles) + static_cast<size_t>(q) * sizeof(h), sizeof(h));
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess || !p) {
+      cudaGetLastError();
+      for (int r = 0; r < q; ++r)
+        if (g->opened[r]) { cudaIpcCloseMemHandle(g->opened[r]); g->opened[r] = nullptr; }
+      return RMSNORM_B200_ERR_CUDA;
+    }
+    g->opened[q] = p;
+    g->recv[q] = reinterpret_cast<unsigned long long*>(static_cast<char*>(p) + kPeerBufferHeader);
+  }
+  g->connected = true;
+  return RMSNORM_B200_OK;
+}
+
+extern "C" int rmsnorm_b200_peer_group_connect_buffers(rmsnorm_b200_peer_group* g, void* const* buffers) {
+  if (!g || !buffers || g->connected) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  for (int q = 0; q < g->world; ++q)
+    if (q != g->rank && !buffers[q]) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  for (int q = 0; q < g->world; ++q)
+    if (q != g->rank)
+      g->recv[q] = reinterpret_cast<unsigned long long*>(static_cast<char*>(buffers[q]) + kPeerBufferHeader);
+  g->connected = true;
+  return RMSNORM_B200_OK;
+}
+
+extern "C" int rmsnorm_b200_peer_group_buffer(rmsnorm_b200_peer_group* g, void** buffer) {
+  if (!g || !buffer) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  *buffer = g->buffer;
+  return RMSNORM_B200_OK;
+}
+
+extern "C" int rmsnorm_b200_peer_group_destroy(rmsnorm_b200_peer_group* g) {
+  if (!g) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  int st = RMSNORM_B200_OK;
+  for (int q = 0; q < g->world; ++q)
+    if (g->opened[q] && cudaIpcCloseMemHandle(g->opened[q]) != cudaSuccess) st = RMSNORM_B200_ERR_CUDA;
+  if (g->buffer && cudaFree(g->buffer) != cudaSuccess) st = RMSNORM_B200_ERR_CUDA;
+  cudaGetLastError();
+  delete g;
+  return st;
+}
+
+extern "C" int rmsnorm_b200_set_peer_timeout_ns(uint64_t timeout_ns) {
+  if (timeout_ns < kMinWaitTimeoutNs) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  unsigned long long v = timeout_ns;
+  if (cudaMemcpyToSymbol(g_peer_timeout_ns, &v, sizeof(v)) != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+  return RMSNORM_B200_OK;
+}
+
+extern "C" int rmsnorm_b200_bwd_allreduce(const rmsnorm_b200_bwd_args* args, void* workspace, size_t workspace_bytes,
+                                          rmsnorm_b200_peer_group* group, void* stream) {
+  if (!group) return RMSNORM_B200_ERR_INVALID_ARGUMENT;
+  return do_bwd(args, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), group);
 }
 
 extern "C" int rmsnorm_b200_bwd_noalloc(const rmsnorm_b200_bwd_args* args, void* stream) {

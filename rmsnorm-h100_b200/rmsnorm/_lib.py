@@ -128,6 +128,20 @@ SIGNATURES = {
     "rmsnorm_b200_abi_version": (ctypes.c_int, []),
     "rmsnorm_b200_max_active_clusters": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]),
     "rmsnorm_b200_launch_count": (ctypes.c_uint64, []),
+    "rmsnorm_b200_peer_buffer_size": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int64, ctypes.POINTER(ctypes.c_size_t)]),
+    "rmsnorm_b200_peer_group_create": (
+        ctypes.c_int,
+        [ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)],
+    ),
+    "rmsnorm_b200_peer_group_connect": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "rmsnorm_b200_peer_group_connect_buffers": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "rmsnorm_b200_peer_group_buffer": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "rmsnorm_b200_peer_group_destroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "rmsnorm_b200_set_peer_timeout_ns": (ctypes.c_int, [ctypes.c_uint64]),
+    "rmsnorm_b200_bwd_allreduce": (
+        ctypes.c_int,
+        [ctypes.POINTER(BwdArgs), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p],
+    ),
     "rmsnorm_b200_last_plan": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_size_t]),
 }
 
@@ -323,19 +337,66 @@ def bwd_workspace_bytes(a: BwdArgs, device: torch.device) -> int:
     return int(n.value)
 
 
-def bwd(a: BwdArgs, device: torch.device, workspace: Optional[torch.Tensor] = None) -> None:
+def bwd(a: BwdArgs, device: torch.device, workspace: Optional[torch.Tensor] = None, peer_group=None) -> None:
     """Enqueues the backward; allocates the workspace from the caching allocator unless
-    one is given."""
+    one is given. With `peer_group` (a handle from peer_group_create), dweight / dbias are
+    summed over the group's ranks by rmsnorm_b200_bwd_allreduce."""
     lib = load_library()
     nbytes = bwd_workspace_bytes(a, device)
     if nbytes and (workspace is None or workspace.numel() < nbytes):
         workspace = torch.empty(nbytes, dtype=torch.uint8, device=device)
     ws_ptr = workspace.data_ptr() if (workspace is not None and nbytes) else None
     with torch.cuda.device(device):
-        _check(
-            lib.rmsnorm_b200_bwd(ctypes.byref(a), ws_ptr, nbytes, _stream_handle(device)),
-            "rmsnorm_b200_bwd",
-        )
+        if peer_group is None:
+            _check(lib.rmsnorm_b200_bwd(ctypes.byref(a), ws_ptr, nbytes, _stream_handle(device)), "rmsnorm_b200_bwd")
+        else:
+            _check(lib.rmsnorm_b200_bwd_allreduce(ctypes.byref(a), ws_ptr, nbytes, peer_group,
+                                                   _stream_handle(device)), "rmsnorm_b200_bwd_allreduce")
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def peer_group_create(device: torch.device, rank: int, world: int, max_grad_floats: int):
+    """(handle, ipc_handle bytes) of this rank's member of a peer group on `device`."""
+    lib = load_library()
+    h = ctypes.c_void_p()
+    ipc = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    with torch.cuda.device(device):
+        _check(lib.rmsnorm_b200_peer_group_create(rank, world, max_grad_floats, ipc, ctypes.byref(h)),
+               "rmsnorm_b200_peer_group_create")
+    return h.value, ipc.raw
+
+
+def peer_group_connect(device: torch.device, handle, ipc_handles) -> None:
+    """Maps the other ranks' buffers (ipc_handles: one bytes object per rank, rank order)."""
+    buf = ctypes.create_string_buffer(b"".join(ipc_handles), IPC_HANDLE_BYTES * len(ipc_handles))
+    with torch.cuda.device(device):
+        _check(load_library().rmsnorm_b200_peer_group_connect(handle, buf), "rmsnorm_b200_peer_group_connect")
+
+
+def peer_group_connect_buffers(device: torch.device, handle, buffers) -> None:
+    """Connects with device pointers for each rank's buffer (rank order; own entry ignored)."""
+    arr = (ctypes.c_void_p * len(buffers))(*[b or 0 for b in buffers])
+    with torch.cuda.device(device):
+        _check(load_library().rmsnorm_b200_peer_group_connect_buffers(handle, arr),
+               "rmsnorm_b200_peer_group_connect_buffers")
+
+
+def peer_group_buffer(handle) -> int:
+    p = ctypes.c_void_p()
+    _check(load_library().rmsnorm_b200_peer_group_buffer(handle, ctypes.byref(p)), "rmsnorm_b200_peer_group_buffer")
+    return int(p.value)
+
+
+def peer_group_destroy(device: torch.device, handle) -> None:
+    with torch.cuda.device(device):
+        _check(load_library().rmsnorm_b200_peer_group_destroy(handle), "rmsnorm_b200_peer_group_destroy")
+
+
+def set_peer_timeout_ns(device: torch.device, ns: int) -> None:
+    with torch.cuda.device(device):
+        _check(load_library().rmsnorm_b200_set_peer_timeout_ns(ns), "rmsnorm_b200_set_peer_timeout_ns")
 
 
 def bwd_noalloc(a: BwdArgs, device: torch.device) -> int:

@@ -3,8 +3,11 @@
 
 Rows are independent in both directions, so every rank owns a contiguous block of rows
 and runs the kernels on it with no communication. The only exchange is in the backward:
-the per-rank dweight / dbias sums are combined with ONE all-reduce (sum, fp32) over NCCL
-(NVLink / NVSwitch). The reference is single-GPU and has no counterpart to this module.
+the per-rank dweight / dbias sums are combined with ONE all-reduce (sum, fp32) over
+NVLink / NVSwitch -- either NCCL's, or, with a `PeerGroup`, the library's own kernel that
+fuses the backward's final reduction with the all-reduce over peer memory (every rank
+pushes its column sums to every rank and sums them in rank order: identical bits on every
+rank). The reference is single-GPU and has no counterpart to this module.
 
 The backward writes its fp32 dweight / dbias sums straight into one packed fp32 buffer
 [dweight | dbias]; the all-reduce sums that buffer in place and each gradient is rounded
@@ -70,6 +73,37 @@ def grad_buffer_numel(x: torch.Tensor, weight: Optional[torch.Tensor], bias: Opt
     return n
 
 
+class PeerGroup:
+    """The library's peer-memory all-reduce for the backward's dweight / dbias, set up over
+    a process group whose ranks are the GPUs of one node (one process per GPU, the current
+    CUDA device of each). Each rank allocates one exchange buffer at set-up (room for
+    `max_grad_floats` gradient values: dweight + dbias elements); the CUDA IPC handles are
+    exchanged once with an all-gather. Every rank must then make the same sequence of
+    backward calls with the same gradient shapes. close() (or the owner's exit) frees it."""
+
+    def __init__(self, max_grad_floats: int, group=None, device: Optional[torch.device] = None):
+        from . import _lib
+
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.max_grad_floats = int(max_grad_floats)
+        self.handle, ipc = _lib.peer_group_create(self.device, self.rank, self.world, self.max_grad_floats)
+        handles: List[Optional[bytes]] = [None] * self.world
+        dist.all_gather_object(handles, ipc, group=group)
+        _lib.peer_group_connect(self.device, self.handle, handles)
+        # every rank has mapped its peers before any rank pushes into them
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        from . import _lib
+
+        if self.handle is not None:
+            torch.cuda.synchronize(self.device)
+            _lib.peer_group_destroy(self.device, self.handle)
+            self.handle = None
+
+
 def rmsnorm_fwd_sharded(x_shard, weight=None, bias=None, residual_shard=None, **kw):
     """Forward on this rank's rows: no communication."""
     return rmsnorm_fwd(x_shard, weight, bias, residual_shard, **kw)
@@ -86,8 +120,10 @@ def rmsnorm_bwd_sharded(
     bias: Optional[torch.Tensor] = None,
     group=None,
     grad_buffer: Optional[torch.Tensor] = None,
+    peer_group: Optional[PeerGroup] = None,
 ) -> Tuple[torch.Tensor, Optional[torch.Tensor], Optional[torch.Tensor], Optional[torch.Tensor]]:
-    """Backward on this rank's rows, then one all-reduce of dweight (+ dbias).
+    """Backward on this rank's rows, then one all-reduce of dweight (+ dbias): NCCL's over
+    `group`, or, with `peer_group` (CUDA tensors), the library's fused kernel.
 
     Returns (dx, dweight, dbias, dresidual) like rmsnorm_bwd: dx and dresidual stay
     sharded, dweight / dbias are the sums over every rank's rows in the affine dtypes (the
@@ -105,9 +141,12 @@ def rmsnorm_bwd_sharded(
     buf = grad_buffer.reshape(-1)[: nw + nb]
     dw32 = buf[:nw].view(dw_shape) if dw_shape is not None else None
     db32 = buf[nw:].view(db_shape) if db_shape is not None else None
+    use_peer = peer_group is not None and x_shard.is_cuda
     dx, dres = _rmsnorm_bwd_fp32_grads(x_shard, weight, dout_shard, rstd_shard, dresidual_out_shard, has_bias,
-                                       has_residual, bias, dw32, db32)
-    if nw + nb and dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+                                       has_residual, bias, dw32, db32,
+                                       peer_group=peer_group.handle if use_peer else None)
+    if (not use_peer and nw + nb and dist.is_available() and dist.is_initialized()
+            and dist.get_world_size(group) > 1):
         dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
     dw = db = None
     if dw32 is not None:

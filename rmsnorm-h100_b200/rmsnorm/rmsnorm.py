@@ -208,9 +208,10 @@ def _db_layout(bias, weight, x, h):
 
 
 def _bwd_cuda(x, weight, dout, rstd, dresidual_out, has_bias, has_residual, bias, h,
-              dx_dtype=None, dresidual_dtype=None, dw_out=None, db_out=None):
+              dx_dtype=None, dresidual_dtype=None, dw_out=None, db_out=None, peer_group=None):
     """dw_out / db_out: caller buffers (any float dtype, the affine shapes) that receive
-    dweight / dbias instead of new tensors in the affine dtypes."""
+    dweight / dbias instead of new tensors in the affine dtypes. peer_group: a native peer
+    group handle; dweight / dbias are then summed over its ranks in the same launch."""
     x_c = _contig(x)
     dout_c = _contig(dout)
     dro_c = _contig(dresidual_out)
@@ -233,7 +234,7 @@ def _bwd_cuda(x, weight, dout, rstd, dresidual_out, has_bias, has_residual, bias
     a = _lib.bwd_args(
         x_c, dout_c, rstd_c, w_c, _heads_of(weight, h), dro_c, dx, dresidual, dw, db, db_heads, h
     )
-    _lib.bwd(a, x.device)
+    _lib.bwd(a, x.device, peer_group=peer_group)
     if has_residual and dresidual is None:
         dresidual = dx
     return dx, dw, db, dresidual
@@ -275,11 +276,13 @@ def _grad_layout(x: Tensor, weight: Optional[Tensor], bias: Optional[Tensor], ha
     return dw_shape, db_shape
 
 
-def _rmsnorm_bwd_fp32_grads(x, weight, dout, rstd, dresidual_out, has_bias, has_residual, bias, dw32, db32):
+def _rmsnorm_bwd_fp32_grads(x, weight, dout, rstd, dresidual_out, has_bias, has_residual, bias, dw32, db32,
+                            peer_group=None):
     """rmsnorm_bwd, except that dweight / dbias are written in fp32 into dw32 / db32
     (fp32 tensors of the shapes _grad_layout gives) whatever the affine dtypes. A
     row-sharded backward sums these per-rank fp32 values across ranks and rounds once to
-    the parameters' dtypes. Returns (dx, dresidual)."""
+    the parameters' dtypes (with `peer_group`, a native peer group handle, the library does
+    that sum itself, in the launch that reduces them). Returns (dx, dresidual)."""
     if x.dtype not in _SUPPORTED_DTYPES:
         raise AssertionError("Unsupported dtype")
     _check_tensor_dtype("Weight", weight)
@@ -299,7 +302,7 @@ def _rmsnorm_bwd_fp32_grads(x, weight, dout, rstd, dresidual_out, has_bias, has_
             db32.copy_(_host.sum_to_affine_shape(g, db32.shape))
         return dx, dres
     dx, _, _, dres = _bwd_cuda(x, weight, dout, rstd, dresidual_out, has_bias, has_residual, bias, h,
-                               dw_out=dw32, db_out=db32)
+                               dw_out=dw32, db_out=db32, peer_group=peer_group)
     return dx, dres
 
 

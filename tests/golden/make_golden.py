@@ -2,7 +2,8 @@
 """Generates tests/golden/*.npz from the REFERENCE package itself.
 
 Run in a container where the reference repository (Int21-AI/RMSNorm-H100) is checked out:
-    python tests/golden/make_golden.py [path/to/reference]    (default: /root/reference)
+    python tests/golden/make_golden.py path/to/reference
+(or with the checkout's path in RMSNORM_REFERENCE_ROOT).
 It imports the reference's `rmsnorm` package and runs its own CPU path (rmsnorm_ref,
 rmsnorm_fwd / rmsnorm_bwd fallbacks, autograd through RMSNormFunction) on seeded inputs
 with the BASELINE distributions, at sizes small enough to commit. The GPU box never runs
@@ -12,6 +13,7 @@ this script; tests only read the .npz files it wrote.
 from __future__ import annotations
 
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -176,4 +178,7 @@ def make_layernorm(ref, eps: float) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("RMSNORM_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py path/to/reference (or set RMSNORM_REFERENCE_ROOT)")
+    main(root)

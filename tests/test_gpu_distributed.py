@@ -42,7 +42,7 @@ def _inputs():
     return x, res, dy, w, b
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, mode="nccl"):
     for p in (str(ROOT), str(ROOT / "rmsnorm-h100_b200")):
         sys.path.insert(0, p)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -59,8 +59,19 @@ def _worker(rank, world, port, q):
         xs, rs, ds = (rd.shard_rows(t, rank, world) for t in (x, res, dy))
         out, ro, rstd = rd.rmsnorm_fwd_sharded(xs, w, b, rs, residual_dtype=torch.float32, store_rstd=True)
         buf = torch.full((rd.grad_buffer_numel(ro, w, b, True),), float("nan"), device=dev)
-        dx, dw, db, _ = rd.rmsnorm_bwd_sharded(ro, w, ds, rstd, has_bias=True, bias=b, grad_buffer=buf)
-        torch.cuda.synchronize(dev)
+        pg = rd.PeerGroup(2 * N) if mode == "peer" else None
+        try:
+            for _ in range(2):  # two steps in a row (the second reuses the exchange buffers)
+                dx, dw, db, _ = rd.rmsnorm_bwd_sharded(ro, w, ds, rstd, has_bias=True, bias=b, grad_buffer=buf,
+                                                       peer_group=pg)
+            torch.cuda.synchronize(dev)
+            if pg is not None:
+                from rmsnorm import _lib
+
+                assert _lib.device_status(dev) == (0, 0)
+        finally:
+            if pg is not None:
+                pg.close()
         s, e = rd.row_range(ROWS, rank, world)
         # numpy arrays travel by value (a tensor's shared-memory handle dies with this process)
         q.put((rank, s, e) + tuple(t.cpu().float().numpy() for t in (out, ro, rstd, dx, dw, db)))
@@ -71,14 +82,17 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_two_gpu_row_sharding_matches_oracle():
+@pytest.mark.parametrize("mode", ["nccl", "peer"])
+def test_two_gpu_row_sharding_matches_oracle(mode):
+    """mode nccl: dweight / dbias summed by NCCL; mode peer: by the library's fused
+    reduction + all-reduce kernel over NVLink peer memory (rmsnorm_b200_bwd_allreduce)."""
     from oracle import rmsnorm_oracle as oracle
 
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     results = sorted((q.get(timeout=300) for _ in range(world)), key=lambda r: r[0])
