@@ -146,7 +146,9 @@ int rmsnorm_b200_bwd(const rmsnorm_b200_bwd_args* args, void* workspace, size_t 
  * reserved by every GPU that loads the library until the process exits. Problems whose
  * partial sums need more return RMSNORM_B200_ERR_SCRATCH_LIMIT without running (every
  * streaming-kernel problem fits on a B200; only very wide rows on the generic path can
- * exceed it). The first call on a device looks up the buffer's device address
+ * exceed it). Where rmsnorm_b200_bwd's plan would keep more partial rows than fit (its
+ * dbias kernels with the sums in tensor memory keep one per row group of every CTA), this
+ * entry point runs the kernels that keep the sums in registers instead. The first call on a device looks up the buffer's device address
  * (cudaGetSymbolAddress); make that first call before any stream capture. All calls on a
  * device share the one buffer, so calls whose kernels overlap on the GPU (different
  * streams, no ordering between them) race and give wrong dweight/dbias; calls ordered on

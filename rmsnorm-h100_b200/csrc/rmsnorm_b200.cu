@@ -929,7 +929,9 @@ bool try_bwd_stream(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdKernel k
   return true;
 }
 
-int plan_bwd(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdPlan* bp) {
+// allow_tmem false: plan without the TMEM-accumulator kernels (their plans can keep more
+// partial rows: one per row group of each of the SM-count CTAs).
+int plan_bwd(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdPlan* bp, bool allow_tmem = true) {
   bp->W = a->hidden * a->heads;
   bp->need_dw = a->dweight != nullptr;
   bp->need_db = a->dbias != nullptr;
@@ -962,7 +964,7 @@ int plan_bwd(DeviceState* ds, const rmsnorm_b200_bwd_args* a, BwdPlan* bp) {
     }
     // dbias backwards: the 4-vector kernel with its sums in TMEM when a row fits one CTA in
     // row mode (up to 16384 columns with 512 threads); the 2-vector register kernel otherwise
-    if (bp->need_db && shape != 2 && env_int("RMSNORM_B200_TMEM_ACC", 1)) {
+    if (bp->need_db && shape != 2 && allow_tmem && env_int("RMSNORM_B200_TMEM_ACC", 1)) {
       if (BwdKernel tk = pick_bwd_tmem(a->x_dtype, a->dout_dtype, a->dx_dtype, dro, dres)) {
         BwdPlan cand = *bp;
         std::string why_t;
@@ -1021,7 +1023,7 @@ int64_t grad_floats(const rmsnorm_b200_bwd_args* a) {
 // group: when not null, the dweight / dbias sums are all-reduced over the group's ranks by
 // the fused reduction kernel instead of reduce_partials_kernel.
 int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream_t stream,
-           rmsnorm_b200_peer_group* group = nullptr) {
+           rmsnorm_b200_peer_group* group = nullptr, bool allow_tmem = true) {
   int st = check_bwd(a);
   if (st) return st;
   if (group != nullptr) {  // checked before anything is launched: the ranks stay in step
@@ -1034,7 +1036,7 @@ int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream
   st = get_device_state(&ds);
   if (st) return st;
   BwdPlan bp;
-  st = plan_bwd(ds, a, &bp);
+  st = plan_bwd(ds, a, &bp, allow_tmem);
   if (st) return st;
   const size_t need = workspace_for(bp);
   if (need > ws_bytes || (need > 0 && (!ws || !aligned16(ws)))) return RMSNORM_B200_ERR_WORKSPACE;
@@ -1265,8 +1267,18 @@ extern "C" int rmsnorm_b200_bwd_noalloc(const rmsnorm_b200_bwd_args* args, void*
   BwdPlan bp;
   st = plan_bwd(ds, args, &bp);
   if (st) return st;
+  // a plan whose partial rows do not fit the buffer falls back to the register-accumulator
+  // kernels, which keep fewer partial rows (one per CTA group instead of one per row group
+  // of every CTA)
+  bool allow_tmem = true;
+  if (workspace_for(bp) > RMSNORM_B200_NOALLOC_SCRATCH_BYTES && bp.tmem) {
+    allow_tmem = false;
+    st = plan_bwd(ds, args, &bp, false);
+    if (st) return st;
+  }
   if (workspace_for(bp) > RMSNORM_B200_NOALLOC_SCRATCH_BYTES) return RMSNORM_B200_ERR_SCRATCH_LIMIT;
-  return do_bwd(args, scratch, RMSNORM_B200_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream));
+  return do_bwd(args, scratch, RMSNORM_B200_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream), nullptr,
+                allow_tmem);
 }
 
 extern "C" const char* rmsnorm_b200_strerror(int status) {

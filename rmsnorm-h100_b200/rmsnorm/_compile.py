@@ -80,30 +80,35 @@ def bwd_op(
         x, weight, dout, rstd, dresidual_out, has_bias, has_residual, bias, h,
         dx_dtype=dx_dtype, dresidual_dtype=dresidual_dtype,
     )
-    empty = x.new_empty(_EMPTY, dtype=torch.float32)
+    def empty():  # a fresh placeholder each time: returns may not alias one another
+        return x.new_empty(_EMPTY, dtype=torch.float32)
+
     return (
         dx,
-        dw if dw is not None else empty,
-        db if db is not None else empty,
-        dres if (dres is not None and dres is not dx) else empty,
+        dw if dw is not None else empty(),
+        db if db is not None else empty(),
+        dres if (dres is not None and dres is not dx) else empty(),
     )
 
 
 @bwd_op.register_fake
 def _(x, weight, dout, rstd, dresidual_out, bias, has_bias, has_residual, dx_dtype, dresidual_dtype):
     h = _api._head_count(weight, bias, x.shape)
-    empty = x.new_empty(_EMPTY, dtype=torch.float32)
+
+    def empty():
+        return x.new_empty(_EMPTY, dtype=torch.float32)
+
     dx = x.new_empty(x.shape, dtype=dx_dtype)
-    dw = weight.new_empty(weight.shape) if weight is not None else empty
+    dw = weight.new_empty(weight.shape) if weight is not None else empty()
     if has_bias:
         db_dtype, db_shape, _ = _api._db_layout(bias, weight, x, h)
         db = x.new_empty(db_shape, dtype=db_dtype)
     else:
-        db = empty
+        db = empty()
     separate = dresidual_out is not None or (
         has_residual and dresidual_dtype is not None and dresidual_dtype != dx_dtype
     )
-    dres = x.new_empty(x.shape, dtype=dresidual_dtype or x.dtype) if separate else empty
+    dres = x.new_empty(x.shape, dtype=dresidual_dtype or x.dtype) if separate else empty()
     return dx, dw, db, dres
 
 
