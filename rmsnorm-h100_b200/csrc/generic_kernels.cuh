@@ -177,10 +177,12 @@ __global__ void __launch_bounds__(kGenericThreads) bwd_generic_partials_kernel(
 // launch reduces both. Narrow rows (per-head backwards: 1024-4096 columns, 148-600 partial
 // rows) have few column blocks, so the rows are spread over 16 warps with eight loads in
 // flight each, which keeps the number of dependent memory round trips per warp small.
-constexpr int kReduceCols = 32;
+constexpr int kReduceCols = 32;    // scalar path: columns per block (one per lane)
+constexpr int kReduceVCols = 128;  // vectorised path: columns per block (four per lane)
 constexpr int kReduceWarps = 16;
 constexpr int kReduceThreads = kReduceCols * kReduceWarps;
-constexpr int kReduceUnroll = 8;
+constexpr int kReduceUnroll = 8;   // scalar path: partial rows in flight per warp
+constexpr int kReduceBatch = 16;   // vectorised path: partial rows in flight per warp
 
 struct ReduceJob {
   const float* part;  // [C][W] partial rows
@@ -197,12 +199,54 @@ struct ReduceParams {
   int64_t N;  // columns of one head
 };
 
+// The vectorised path applies to a job without folded heads whose partial rows are
+// 16-byte aligned and a multiple of 4 columns wide (the streaming kernels' partials).
+__host__ __device__ __forceinline__ bool reduce_vectorised(const ReduceJob& jb, int64_t W) {
+  return jb.fold == 1 && (W & 3) == 0 && (reinterpret_cast<uintptr_t>(jb.part) & 15u) == 0;
+}
+
+// Fixed-order column sums of the partial rows: warp w sums rows w, w + 16, ... in
+// ascending order, then the 16 warp sums are added in warp order -- the same bits every
+// run. Vectorised path: lane l owns columns 4l .. 4l + 3 of a 128-column block and a warp
+// keeps up to kReduceBatch partial rows' loads in flight (the partial rows were just
+// written by the backward and mostly sit in L2, so the sum is latency-bound; one batch
+// covers the 148-600 rows of a streaming backward in about one round trip).
 __global__ void __launch_bounds__(kReduceThreads) reduce_partials_kernel(const ReduceParams p) {
-  __shared__ float acc_w[kReduceWarps][kReduceCols];
+  __shared__ float acc_w[kReduceWarps][kReduceVCols];
   const ReduceJob& jb = blockIdx.y == 0 ? p.job[0] : p.job[1];  // no dynamic index into the parameters
-  if (static_cast<int64_t>(blockIdx.x) * kReduceCols >= jb.wout) return;  // whole block idle
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  if (reduce_vectorised(jb, p.W)) {
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kReduceVCols;
+    if (base >= jb.wout) return;  // whole block idle
+    const int64_t j = base + 4 * lane;  // all four columns valid or none (wout % 4 == 0)
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (j < jb.wout) {
+      const float* col = jb.part + j;
+      for (int64_t c0 = warp; c0 < p.C; c0 += kReduceWarps * kReduceBatch) {
+        float4 v[kReduceBatch];
+#pragma unroll
+        for (int u = 0; u < kReduceBatch; ++u) {
+          const int64_t c = c0 + u * kReduceWarps;
+          v[u] = c < p.C ? *reinterpret_cast<const float4*>(col + c * p.W) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kReduceBatch; ++u) {
+          acc.x += v[u].x; acc.y += v[u].y; acc.z += v[u].z; acc.w += v[u].w;
+        }
+      }
+    }
+    *reinterpret_cast<float4*>(&acc_w[warp][4 * lane]) = acc;
+    __syncthreads();
+    if (threadIdx.x < kReduceVCols && base + threadIdx.x < jb.wout) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kReduceWarps; ++w) t += acc_w[w][threadIdx.x];
+      store1_rt(jb.out, jb.out_dt, base + threadIdx.x, t);
+    }
+    return;
+  }
+  if (static_cast<int64_t>(blockIdx.x) * kReduceCols >= jb.wout) return;  // whole block idle
   const int64_t j = static_cast<int64_t>(blockIdx.x) * kReduceCols + lane;
   float acc = 0.f;
   if (j < jb.wout) {

@@ -33,7 +33,7 @@ constexpr int kARBlocks = 128;   // CTAs of every call (the tag derivation relie
 constexpr int kARThreads = 512;
 constexpr int kARWarps = kARThreads / 32;
 constexpr int kARCols = 128;     // output columns per column block (4 per lane)
-constexpr int kARUnroll = 8;     // partial rows in flight per warp
+constexpr int kARUnroll = 16;    // partial rows in flight per warp
 constexpr int kMaxPeers = 8;
 constexpr unsigned long long kPeerBufferHeader = 256;  // bytes before the receive area (the call counter)
 
@@ -79,26 +79,23 @@ __global__ void __launch_bounds__(kARThreads, 1) reduce_allreduce_kernel(const R
     const ReduceJob& jb = jidx == 0 ? rp.job[0] : rp.job[1];
     const int64_t base = (b < nb0 ? b : b - nb0) * kARCols;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    const bool vec = jb.fold == 1 && (rp.W & 3) == 0 && (reinterpret_cast<uintptr_t>(jb.part) & 15u) == 0;
+    const bool vec = reduce_vectorised(jb, rp.W);
     if (vec) {
       // lane l: columns base + 4l .. base + 4l + 3 (whole or none: W and wout are multiples of 4)
       const int64_t j = base + 4 * lane;
       if (j < jb.wout) {
         const float* col = jb.part + j;
-        int64_t c = warp;
-#pragma unroll 1
-        for (; c + (kARUnroll - 1) * kARWarps < rp.C; c += kARUnroll * kARWarps) {
-          float4 v[kARUnroll];
+        for (int64_t c0 = warp; c0 < rp.C; c0 += kARWarps * kARUnroll) {
+          float4 v[kARUnroll];  // all of a warp's rows in flight at once (typically one batch)
 #pragma unroll
-          for (int u = 0; u < kARUnroll; ++u) v[u] = *reinterpret_cast<const float4*>(col + (c + u * kARWarps) * rp.W);
+          for (int u = 0; u < kARUnroll; ++u) {
+            const int64_t c = c0 + u * kARWarps;
+            v[u] = c < rp.C ? *reinterpret_cast<const float4*>(col + c * rp.W) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
 #pragma unroll
           for (int u = 0; u < kARUnroll; ++u) {
             acc[0] += v[u].x; acc[1] += v[u].y; acc[2] += v[u].z; acc[3] += v[u].w;
           }
-        }
-        for (; c < rp.C; c += kARWarps) {
-          const float4 v = *reinterpret_cast<const float4*>(col + c * rp.W);
-          acc[0] += v.x; acc[1] += v.y; acc[2] += v.z; acc[3] += v.w;
         }
       }
 #pragma unroll

@@ -1086,7 +1086,6 @@ int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream
   rp.W = bp.W;
   rp.N = a->hidden;
   int njobs = 0;
-  int64_t max_wout = 0;
   auto add_job = [&](const float* part, void* outp, int out_dt, int out_heads) {
     ReduceJob& jb = rp.job[njobs++];
     jb.fold = (out_heads == 1 && a->heads > 1) ? a->heads : 1;
@@ -1094,7 +1093,6 @@ int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream
     jb.part = part;
     jb.out = outp;
     jb.out_dt = out_dt;
-    max_wout = std::max(max_wout, jb.wout);
   };
   if (a->dweight) add_job(dw_part, a->dweight, a->dweight_dtype, a->weight_heads);
   if (a->dbias) add_job(db_part, a->dbias, a->dbias_dtype, a->dbias_heads);
@@ -1110,7 +1108,12 @@ int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream
     g_launches.fetch_add(1, std::memory_order_relaxed);
     t_last_plan += " allreduce=peer world=" + std::to_string(group->world);
   } else if (njobs > 0) {
-    const dim3 grid(static_cast<unsigned>((max_wout + kReduceCols - 1) / kReduceCols), static_cast<unsigned>(njobs));
+    int64_t blocks = 0;  // column blocks of the widest job (per-job block width: see reduce_vectorised)
+    for (int i = 0; i < njobs; ++i) {
+      const int64_t cols = reduce_vectorised(rp.job[i], rp.W) ? kReduceVCols : kReduceCols;
+      blocks = std::max(blocks, (rp.job[i].wout + cols - 1) / cols);
+    }
+    const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(njobs));
     reduce_partials_kernel<<<grid, kReduceThreads, 0, stream>>>(rp);
     if (cudaGetLastError() != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
     g_launches.fetch_add(1, std::memory_order_relaxed);
