@@ -974,7 +974,7 @@ def main():
             "parity": parity,
             "roofline": {"bound": "hbm", "kernel": kern_name, "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic_for(args.workload),
+                         "traffic": None if (args.rows or args.hidden) else traffic_for(args.workload),
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6.65 TB/s", "kernel_ms": round(kern_ms, 5),
                          "bytes_per_launch": kern_bytes},
