@@ -161,6 +161,28 @@ __device__ __forceinline__ float group_take(const StreamPlan& pl, const SmemLayo
   return warp_sum(lane < nw ? L.gpart[j * 16 + gid * nw + lane] : 0.f);
 }
 
+// Combining (mean, M2 = sum of squared deviations) of two sets of c samples each (Chan et
+// al.'s parallel variance update with equal counts): mean = (m_a + m_b) / 2, M2 = M2_a +
+// M2_b + (m_b - m_a)^2 c / 2. It is symmetric in its two operands (a + b, the square of a
+// difference), so the lanes of an xor butterfly all end with identical bits, and it needs
+// no division. `c` doubles at every level.
+__device__ __forceinline__ void stats_combine_equal(float& m, float& M2, float mo, float M2o, float c) {
+  const float d = mo - m;
+  M2 = (M2 + M2o) + d * d * (0.5f * c);
+  m = (m + mo) * 0.5f;
+}
+
+// Butterfly over lanes [0, width) (width a power of two): every lane ends with the (mean,
+// M2) of the width lanes' sets of c samples each.
+__device__ __forceinline__ void lanes_stats(float& m, float& M2, float c, int width) {
+  for (int off = width >> 1; off > 0; off >>= 1) {
+    const float mo = __shfl_xor_sync(0xffffffffu, m, off);
+    const float M2o = __shfl_xor_sync(0xffffffffu, M2, off);
+    stats_combine_equal(m, M2, mo, M2o, c);
+    c *= 2.f;
+  }
+}
+
 // Cluster exchange of a row total (rows split over the P CTAs of a cluster, one row group
 // per CTA). cluster_send (warp 0): lane 0 stores this CTA's total locally and arms the
 // slot's mbarrier for the P-1 peer totals; lane q != rank stores it into peer q's slot with
@@ -691,6 +713,94 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
         if (release_slot(L, s, nwarps) && q + S < n_local) issue_unit(q + S, s);
         if (++s == S) { s = 0; ph ^= 1u; }
       }
+    }
+  } else if (active_warp && ln_rows && pl.vslice == G * kVecs && ((G >> 5) & ((G >> 5) - 1)) == 0) {
+    // --------- LayerNorm rows, pipelined, statistics in one pass ---------
+    // Every thread holds whole vectors of the row (a full slice, so every thread and every
+    // warp of the group has the same sample count; a power-of-two number of warps) and
+    // computes the mean and the sum of squared deviations (M2) of its 8 * kVecs values in
+    // one read of shared memory; the warp and then the row group combine them
+    // (stats_combine_equal). Iteration
+    // q: statistics of row q, posted; output of row q-1 once its statistics are in. Slots
+    // are used by row mod 4 (a warp posts row q after taking row q-1, as in the RMSNorm
+    // pipelined loop); the mean of each warp goes to gpart, its M2 to xpart (unused:
+    // LayerNorm rows are never split).
+    int s = 0, sp = 0;
+    uint32_t ph = 0;
+    bool act_p = false;
+    int64_t row_p = 0;
+    const X* xs_p = nullptr;
+    const int nw = G >> 5;
+    const float n_warp = static_cast<float>(8 * kVecs * 32);
+    for (int64_t q = 0; q <= n_local; ++q) {
+      bool act_q = false;
+      int64_t row_q = 0;
+      const X* xs_q = nullptr;
+      const uint32_t slot = static_cast<uint32_t>(q) & 3u;
+      if (q < n_local) {
+        mbar_wait(&L.full[s], ph, kSiteFwdFull);
+        const int64_t row0 = (cid + q * ncl) * pl.R;
+        act_q = in_group && row0 + gid < pl.nrows;
+        row_q = row0 + gid;
+        xs_q = stage_x(s) + gid * xs_stride;
+        float m = 0.f, M2 = 0.f;
+        if (act_q) {
+          // one read of the thread's 8 * kVecs values: sums of d = x - x0 and d^2, shifted
+          // by the thread's first value x0 so that M2 = S2 - S1^2 / n cancels at most within
+          // the thread's own values (every deviation is measured from one of them)
+          float2 h[4];
+          Pair8<X>::load(xs_q, h);
+          const float x0 = h[0].x;
+          const float2 sh = splat2(-x0);
+          float2 s1 = splat2(0.f), s2 = splat2(0.f);
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) {
+            if (k > 0) Pair8<X>::load(xs_q + k * G8, h);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 d = add2(h[i], sh);
+              s1 = add2(s1, d);
+              s2 = fma2(d, d, s2);
+            }
+          }
+          const float S1 = s1.x + s1.y;
+          const float S2 = s2.x + s2.y;
+          constexpr float kInvN = 1.f / static_cast<float>(8 * kVecs);
+          m = fmaf(S1, kInvN, x0);
+          M2 = fmaxf(fmaf(-S1, S1 * kInvN, S2), 0.f);
+        }
+        lanes_stats(m, M2, static_cast<float>(8 * kVecs), 32);
+        if (lane == 0) {
+          L.gpart[slot * 16 + warp] = m;
+          L.xpart[slot * 16 + warp] = M2;
+          mbar_arrive(&L.gbar[gid * kGroupRed + slot]);
+        }
+      }
+      if (q >= 1) {
+        const uint32_t ps = (slot + 3u) & 3u;
+        mbar_wait(&L.gbar[gid * kGroupRed + ps], static_cast<uint32_t>((q - 1) >> 2) & 1u, kSiteFwdCluster);
+        float m = L.gpart[ps * 16 + gid * nw + (lane & (nw - 1))];
+        float M2 = L.xpart[ps * 16 + gid * nw + (lane & (nw - 1))];
+        lanes_stats(m, M2, n_warp, nw);  // every lane combines the group's nw warps
+        const float rstd = rsqrtf(M2 * inv_n + p.eps);  // m, M2: row q-1's mean and M2
+        if (act_p) {
+          OT* op = static_cast<OT*>(p.out) + row_p * pl.W + gl * 8;
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) ln_emit(xs_p + k * G8, op + k * G8, m, rstd, k);
+          if (gl == 0) {
+            if (p.rstd != nullptr) p.rstd[row_p] = rstd;
+            if (p.mean != nullptr) p.mean[row_p] = m;
+          }
+        }
+        if (release_slot(L, sp, nwarps) && q - 1 + S < n_local) issue_unit(q - 1 + S, sp);
+      }
+      if (q < n_local) {
+        sp = s;
+        if (++s == S) { s = 0; ph ^= 1u; }
+      }
+      act_p = act_q;
+      row_p = row_q;
+      xs_p = xs_q;
     }
   } else if (active_warp && ln_rows) {
     // --------- LayerNorm rows, pipelined one tile deep (tiles hold one row per group) ---------
