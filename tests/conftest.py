@@ -43,3 +43,26 @@ def golden():
 
 def cuda_available() -> bool:
     return torch.cuda.is_available()
+
+
+@pytest.fixture(autouse=True)
+def _nan_poisoned_device_memory(request):
+    """Before every GPU test, the caching allocator's free device memory is filled with 0xFF
+    bytes -- NaN as fp16, bf16 and fp32 -- so an output element a kernel fails to write
+    reads NaN instead of a value an earlier test left in the same block. One large segment
+    (a quarter of the free memory, at most 16 GiB) serves the tensors the API allocates;
+    a few small ones serve allocations under 1 MiB, which the allocator keeps apart."""
+    if request.node.get_closest_marker("gpu") is None or not torch.cuda.is_available():
+        yield
+        return
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    free, _ = torch.cuda.mem_get_info()
+    big = torch.empty(min(free // 4, 16 << 30), dtype=torch.uint8, device="cuda")
+    big.fill_(0xFF)
+    small = [torch.empty((1 << 20) - 512, dtype=torch.uint8, device="cuda") for _ in range(16)]
+    for t in small:
+        t.fill_(0xFF)
+    torch.cuda.synchronize()
+    del big, small
+    yield
