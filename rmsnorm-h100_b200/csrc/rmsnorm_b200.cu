@@ -302,6 +302,7 @@ bool make_stream_plan(int64_t rows, int64_t N64, int H, const int in_bytes[3], b
   pl.rps = P > 1 ? 1 : T / pl.G;
   if (pl.rps < 1) { *why = "group wider than the CTA"; return false; }
   pl.lag = 0;
+  pl.xpair = 0;
   pl.K = 1;
   pl.kpc_shift = log2i(max_vecs);
 
@@ -429,11 +430,11 @@ std::string describe(const char* kind, const StreamPlan& pl, int grid) {
   char buf[512];
   std::snprintf(buf, sizeof(buf),
                 "%s mode=%s P=%d x=%s grid=%d clusters=%d T=%d G=%d rps=%d R=%d S=%d stage=%u "
-                "vslice=%d vs=%d cols=%d K=%d lag=%d pf=%d tiles=%lld",
+                "vslice=%d vs=%d cols=%d K=%d lag=%d%s pf=%d tiles=%lld",
                 kind, pl.seg_mode ? "seg" : "row", pl.P,
                 pl.P == 1 ? "none" : (pl.xmode == kXGlobal ? "global" : "cluster"), grid, pl.nclusters, pl.T, pl.G,
                 pl.rps,
-                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, pl.cols, pl.K, pl.lag, pl.pf,
+                pl.R, pl.S, pl.stage_bytes, pl.vslice, pl.vs, pl.cols, pl.K, pl.lag, pl.xpair ? " pairs" : "", pl.pf,
                 static_cast<long long>(pl.ntiles));
   return buf;
 }
@@ -794,6 +795,16 @@ int do_fwd(const rmsnorm_b200_fwd_args* a, cudaStream_t stream) {
       planned = make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, false, kMaxVecs, kLarge,
                                  env_int("RMSNORM_B200_FORCE_CLUSTER", 0), &pl, &why);
     if (planned) {
+      // Split rows over 2 or 4 CTAs whose ring holds two pairs of row slices and two more
+      // loading go in pairs. Measured on B200 (bf16, CUDA-graph replays, interleaved A/B):
+      // P = 2 +11.6 %, P = 4 +5 %, but P = 8 -6.7 % and P = 16 -6 %, where each pair's
+      // exchange waits on the records of twice as many CTAs.
+      if (pl.P > 1 && pl.K == 1 && pl.P <= 4 && pl.S >= 6 && !a->residual && !a->residual_out &&
+          env_int("RMSNORM_B200_XPAIR", 1) &&
+          env_int("RMSNORM_B200_FORCE_LAG", -1) < 0) {
+        pl.xpair = 1;
+        pl.lag = 1;
+      }
       FwdParams p = {};
       p.x = a->x; p.res = a->residual; p.w = a->weight; p.b = a->bias;
       p.out = a->out; p.ro = a->residual_out; p.rstd = a->rstd;

@@ -289,6 +289,69 @@ __device__ __forceinline__ float cluster_recv(const StreamPlan& pl, const SmemLa
   return warp_sum(lane < pl.P ? xp[lane] : 0.f);
 }
 
+// Row pairs (forward split rows, P <= 16): the records of rows seq_a (lanes 0..15) and
+// seq_a + 1 (lanes 16..31), lane q of each half reading CTA q's record.
+__device__ __forceinline__ XRecord xrec_load2(const StreamPlan& pl, const XCtx& xc, int lane, uint32_t seq_a) {
+  const int q = lane & 15;
+  if (pl.xmode != kXGlobal || q >= pl.P) return 0ull;
+  const uint32_t seq = seq_a + static_cast<uint32_t>(lane >> 4);
+  return ld_relaxed_u64(xc.rec + (xc.cta0 + q) * kXSlots + (seq & (kXSlots - 1)));
+}
+
+// Group totals of rows seq_a and (hb) seq_a + 1. Global records: one bounded poll of both
+// rows' records (`pre`: this lane's xrec_load2), then the half-warp sums. warp_sum over a
+// row's P values in lanes 0..P-1 adds zeros at its first level (offset 16) and then runs
+// offsets 8..1 over the 16 lanes, so the 16-lane sums here give the same bits as
+// cluster_recv. Cluster exchange: the two rows one after the other.
+__device__ __forceinline__ void cluster_recv2(const StreamPlan& pl, const SmemLayout& L, const XCtx& xc, int lane,
+                                              uint32_t seq_a, bool hb, XRecord pre, int site, float& ta, float& tb) {
+  if (pl.xmode == kXGlobal) {
+    const bool mine = (lane & 15) < pl.P && (lane < 16 || hb);
+    const uint32_t want = xrec_tag(pl, seq_a + static_cast<uint32_t>(lane >> 4));
+    XRecord w = pre;
+    uint64_t t0 = 0;
+    while (!__all_sync(0xffffffffu, !mine || static_cast<uint32_t>(w >> 32) == want)) {
+      if (abort_requested()) break;
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > g_wait_timeout_ns) {
+        if (lane == 0) record_error(RMSNORM_B200_ERR_DEVICE_TIMEOUT, site);
+        break;
+      }
+      __nanosleep(20);
+      w = xrec_load2(pl, xc, lane, seq_a);
+    }
+    float v = mine ? __uint_as_float(static_cast<uint32_t>(w)) : 0.f;
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    ta = __shfl_sync(0xffffffffu, v, 0);
+    tb = __shfl_sync(0xffffffffu, v, 16);
+    return;
+  }
+  ta = cluster_recv(pl, L, xc, lane, seq_a, 0ull, site);
+  tb = hb ? cluster_recv(pl, L, xc, lane, seq_a + 1, 0ull, site) : 0.f;
+}
+
+// Two rows' CTA-wide sums behind one barrier (split rows: one row group, gid 0). `buf`
+// holds 64 floats (row a's warp partials, then row b's), double-buffered by the caller.
+// The arithmetic is group_sum's, row by row.
+__device__ __forceinline__ void group_sum2(float& a, float& b, const StreamPlan& pl, float* buf, int gl) {
+  a = warp_sum(a);
+  b = warp_sum(b);
+  if (pl.G > 32) {
+    const int nw = pl.G >> 5;
+    const int lane = gl & 31;
+    if (lane == 0) {
+      buf[gl >> 5] = a;
+      buf[32 + (gl >> 5)] = b;
+    }
+    named_barrier(1, pl.G);
+    a = warp_sum(lane < nw ? buf[lane] : 0.f);
+    b = warp_sum(lane < nw ? buf[32 + lane] : 0.f);
+  }
+}
+
 // xor-shuffle sum over aligned groups of `width` lanes (width a power of two <= 32).
 __device__ __forceinline__ float seg_sum(float v, int width, unsigned mask) {
   for (int off = width >> 1; off > 0; off >>= 1) v += __shfl_xor_sync(mask, v, off);
@@ -1003,6 +1066,67 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       if (release_slot(L, s, nwarps) && q + S < n_local)
         issue_unit(q + S, s);
       if (++s == S) { s = 0; ph ^= 1u; }
+    }
+  } else if (!kRes && !kRO && active_warp && !kLN && pl.xpair) {
+    // --------- split-row loop over row pairs (one row per tile, K = 1) ---------
+    // Iteration j: pass 1 of local rows 2j and 2j+1, both CTA sums behind one barrier, both
+    // sent; then both totals of pair j-1 received in one poll and their pass 2. A row slice
+    // of 32 KB streams in about 1.5 us per SM at full HBM bandwidth, about what the fixed
+    // per-row costs (CTA barrier, exchange round trip, record poll) took by themselves;
+    // pairs pay them once per two rows. Sums are formed as in the row-by-row loop, so the
+    // results are the same. The ring holds pairs j and j-1 (planned for S >= 6; compiled
+    // into the residual-free kernels only, whose registers leave room for it). Record
+    // slots (row mod 8): a CTA sends pair j after receiving pair j-2, which needed every
+    // peer's send of pair j-2, made after that peer received pair j-4 (the rows whose
+    // slots pair j reuses).
+    int s1 = 0, s2 = 0;
+    uint32_t ph1 = 0;
+    const int64_t npairs = (n_local + 1) >> 1;
+    for (int64_t j = 0; j <= npairs; ++j) {
+      const int64_t ra2 = 2 * (j - 1);  // pair j-1's first row
+      const XRecord pre = j >= 1 ? xrec_load2(pl, xc, lane, static_cast<uint32_t>(ra2)) : 0ull;
+      if (j < npairs) {
+        const int64_t ra = 2 * j;
+        const bool hb = ra + 1 < n_local;
+        float pa[kVecs], pb[kVecs];
+        mbar_wait(&L.full[s1], ph1, kSiteFwdFull);
+        pass1(stage_x(s1), stage_r(s1), pa);
+        if (++s1 == S) { s1 = 0; ph1 ^= 1u; }
+        if (hb) {
+          mbar_wait(&L.full[s1], ph1, kSiteFwdFull);
+          pass1(stage_x(s1), stage_r(s1), pb);
+          if (++s1 == S) { s1 = 0; ph1 ^= 1u; }
+        } else {
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) pb[k] = 0.f;
+        }
+        float ssa = 0.f, ssb = 0.f;
+#pragma unroll
+        for (int k = 0; k < kVecs; ++k) {
+          ssa += pa[k];
+          ssb += pb[k];
+        }
+        group_sum2(ssa, ssb, pl, (j & 1) ? L.gpart : L.red, gl);
+        cluster_send(ssa, pl, L, xc, warp, lane, static_cast<uint32_t>(ra), rank);
+        if (hb) cluster_send(ssb, pl, L, xc, warp, lane, static_cast<uint32_t>(ra + 1), rank);
+      }
+      if (j >= 1) {
+        const bool hb = ra2 + 1 < n_local;
+        float tot[2];
+        cluster_recv2(pl, L, xc, lane, static_cast<uint32_t>(ra2), hb, pre, kSiteFwdCluster, tot[0], tot[1]);
+        for (int h = 0; h < (hb ? 2 : 1); ++h) {
+          const int64_t r2 = ra2 + h;
+          const int64_t row = cid + r2 * ncl;
+          float rstd_k[kVecs];
+          const float rs = rsqrtf(fmaf(tot[h], inv_n, p.eps));
+#pragma unroll
+          for (int k = 0; k < kVecs; ++k) rstd_k[k] = rs;
+          if (in_group) pass2(stage_x(s2), stage_r(s2), row, rstd_k);
+          if (p.rstd != nullptr && tid == 0 && rank == 0) p.rstd[row] = rs;
+          if (release_slot(L, s2, nwarps) && r2 + S < n_local) issue_unit(r2 + S, s2);
+          if (++s2 == S) s2 = 0;
+        }
+      }
     }
   } else if (active_warp && !kLN) {
     // --------- split-row loop (rows split over the cluster, one row per tile) ---------

@@ -39,6 +39,8 @@ struct StreamPlan {
   int32_t pipe_rows;  // RMSNorm row mode: rows pipelined one tile deep (ring holds one more slot)
   int32_t lag;        // rows the cluster exchange lags pass 1 by (P > 1): pass 2 of row i-lag
                       // follows pass 1 of row i
+  int32_t xpair;      // forward split rows: rows go in pairs (one CTA-wide sum, one exchange
+                      // round and one record poll per two rows); lag = 1 pair, K = 1
   int32_t cols;       // thread vectors (columns) per super-row in a sweep: the kernel's vectors
                       // per thread, or fewer in per-head column mode (each thread then covers
                       // kVecs / cols super-rows of the sweep)

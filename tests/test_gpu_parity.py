@@ -566,6 +566,36 @@ def test_split_row_pipeline_variants(monkeypatch, k, lag, dtype):
             assert "P=" in plan and f"K={k}" in plan, plan
 
 
+@pytest.mark.parametrize("xmode", ["0", "1"])
+@pytest.mark.parametrize("rows,n,dtype", [(1, 65536, BF16), (74, 65536, BF16), (111, 65536, BF16),
+                                           (301, 65536, F16), (148, 32768, BF16), (222, 32768, F16),
+                                           (1001, 65536, F16)])
+def test_split_row_pairs_match_row_by_row(monkeypatch, xmode, rows, n, dtype):
+    """Residual-free forwards with rows split over 2 or 4 CTAs take their rows in pairs (one
+    CTA-wide sum, one exchange round and one record poll per two rows). With odd and even
+    row counts per CTA (1, 2, 3 and more), cluster and global exchange, out and rstd must
+    equal the row-by-row loop's bit for bit and match the oracle."""
+    monkeypatch.setenv("RMSNORM_B200_XMODE", xmode)
+    x = _g((rows, n), dtype, 400 + rows)
+    w = _g((n,), F32, 401, "weight")
+    b = _g((n,), F32, 402, "bias")
+    out_p, _, rstd_p = rmsnorm.rmsnorm_fwd(x, w, b, None, store_rstd=True)
+    torch.cuda.synchronize()
+    plan = _lib.last_plan()
+    assert "pairs" in plan and ("x=global" in plan) == (xmode == "1"), plan
+    monkeypatch.setenv("RMSNORM_B200_XPAIR", "0")
+    out_r, _, rstd_r = rmsnorm.rmsnorm_fwd(x, w, b, None, store_rstd=True)
+    torch.cuda.synchronize()
+    assert "pairs" not in _lib.last_plan(), _lib.last_plan()
+    assert torch.equal(out_p.view(torch.int16), out_r.view(torch.int16)), plan
+    assert torch.equal(rstd_p, rstd_r), plan
+    idx = torch.arange(0, rows, max(1, rows // 16))
+    _, _, o_rstd, y = oracle.fwd(x[idx].cpu(), w.cpu(), b.cpu(), None)
+    oracle.check_close(out_p[idx], y, dtype, f"pairs out [{plan}]")
+    assert torch.allclose(rstd_p[idx].cpu(), o_rstd, rtol=1e-5, atol=0), plan
+    assert _lib.device_status(DEV) == (0, 0)
+
+
 def test_split_row_global_exchange_concurrent_streams(monkeypatch):
     """Two split-row launches with the global-memory exchange running at the same time on
     two streams (launch epochs pick different record sets) give the same bits as the same
