@@ -27,6 +27,10 @@
  *   rmsnorm_b200_abi_version, rmsnorm_b200_launch_count, rmsnorm_b200_last_plan,
  *   rmsnorm_b200_max_active_clusters
  *                           <- no counterpart (introspection for tests and benchmarks).
+ *   rmsnorm_b200_debug_bounds_build, rmsnorm_b200_debug_report
+ *                           <- no counterpart: the bounds-checked build's report (the
+ *                              reference's only memory check was its standalone verifier's
+ *                              element-wise compare, ptx_rmsnorm_kernels.cu:6723-6787).
  *
  * Semantics (identical to the reference's fp32 math, rmsnorm/rmsnorm.py:230-271, 390-399):
  *   rows are the flattened leading dimensions; row r uses affine head (r % heads).
@@ -253,6 +257,22 @@ int rmsnorm_b200_set_wait_timeout_ns(uint64_t timeout_ns);
 int rmsnorm_b200_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
 
 int rmsnorm_b200_abi_version(void);
+
+/* Bounds-checked build (librmsnorm_b200_debug.so, compiled with -DRMSB_DEBUG_BOUNDS; a
+ * stand-in for a memory checker, not for production). Every API call registers the byte
+ * ranges of its tensors, workspace and internal arrays; every load, store and copy of its
+ * kernels checks its bytes against them (global memory) or against the end of the CTA's
+ * shared memory, and a failed check is counted, the first one recorded, and the access
+ * skipped (loads read zeros; nothing traps). rmsnorm_b200_debug_bounds_build returns 1 in
+ * that build and 0 otherwise. rmsnorm_b200_debug_report synchronises `stream` and returns
+ * the number of failed checks since the last clear and the first one's site (1 vector
+ * load, 2 vector store, 3 bulk-copy source, 4 bulk-copy destination, 5 async copy, 6
+ * scalar load, 7 scalar store, 8 exchange record, 9 peer word, 10 partial-row load, 11 L2
+ * prefetch), address and size; clear != 0 resets them. The release build returns
+ * RMSNORM_B200_ERR_UNSUPPORTED. */
+int rmsnorm_b200_debug_bounds_build(void);
+int rmsnorm_b200_debug_report(void* stream, uint64_t* violations, int32_t* site, uint64_t* address,
+                              uint32_t* bytes, int32_t clear);
 
 /* How many clusters of `cluster_size` CTAs of the streaming kernels (512 threads, the full
  * shared-memory carve-out) the current device can hold at once; 1 CTA per SM. Used by the

@@ -50,6 +50,96 @@ __device__ __forceinline__ void record_error(int code, int where) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Dynamic shared memory of the streaming kernels (every extern __shared__ array aliases its
+// start).
+extern __shared__ __align__(128) unsigned char rmsb_dyn_smem[];
+
+// ---------------------------------------------------------------------------------------
+// Bounds-checked build (compiled with -DRMSB_DEBUG_BOUNDS into librmsnorm_b200_debug.so;
+// the stand-in for a memory checker). Every API call registers the byte ranges of its
+// tensors, workspace and internal arrays (g_dbg_ranges, written by a one-thread kernel
+// ahead of the call's kernels on the same stream). Each vector / scalar load and store,
+// bulk copy (source and shared-memory destination), async copy and exchange access then
+// checks its bytes: global addresses must lie inside one registered range, shared
+// addresses below the end of the CTA's dynamic shared memory. A failed check records the
+// first bad access (site, address, size) and the count in g_dbg_report and SKIPS the
+// access (loads read zeros; a skipped bulk copy still completes its bytes on the
+// mbarrier, so no wait hangs). Nothing traps. Runs of non-bulk async copies are checked as
+// a whole before the first copy (and are plain copies in this build: see cp_async_4). In the release build every check is the
+// constant true and compiles away.
+// ---------------------------------------------------------------------------------------
+enum DbgSite : int {
+  kDbgVecLoad = 1,
+  kDbgVecStore = 2,
+  kDbgBulkSrc = 3,
+  kDbgBulkDst = 4,
+  kDbgAsyncCopy = 5,
+  kDbgScalarLoad = 6,
+  kDbgScalarStore = 7,
+  kDbgRecord = 8,
+  kDbgPeerWord = 9,
+  kDbgPartialLoad = 10,
+  kDbgPrefetch = 11,
+};
+constexpr int kDbgMaxRanges = 24;
+struct DbgRanges {
+  int32_t n;
+  int32_t clip_site;  // unused by the device; keeps the layout 8-byte aligned
+  unsigned long long lo[kDbgMaxRanges];
+  unsigned long long hi[kDbgMaxRanges];
+};
+
+#ifdef RMSB_DEBUG_BOUNDS
+__device__ DbgRanges g_dbg_ranges;
+__device__ unsigned long long g_dbg_report[4];  // violations, first site, first address, first size
+
+__device__ __noinline__ bool dbg_check(const void* p, uint32_t bytes, int site) {
+  const unsigned long long a = reinterpret_cast<unsigned long long>(p);
+  bool ok = true;
+  if (__isShared(p)) {
+    uint32_t dyn;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+    const uint32_t off = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+    const uint32_t end = static_cast<uint32_t>(__cvta_generic_to_shared(rmsb_dyn_smem)) + dyn;
+    ok = off + bytes <= end;
+  } else if (__isGlobal(p)) {
+    ok = false;
+    const int n = g_dbg_ranges.n;
+    for (int i = 0; i < n && i < kDbgMaxRanges; ++i)
+      if (a >= g_dbg_ranges.lo[i] && a + bytes <= g_dbg_ranges.hi[i]) ok = true;
+  }
+  if (!ok && atomicAdd(&g_dbg_report[0], 1ull) == 0) {
+    g_dbg_report[1] = static_cast<unsigned long long>(site);
+    g_dbg_report[2] = a;
+    g_dbg_report[3] = bytes;
+  }
+  return ok;
+}
+
+__global__ void dbg_ranges_kernel(const DbgRanges r) {
+  if (threadIdx.x == 0) g_dbg_ranges = r;
+}
+#define RMSB_DBG_OK(p, bytes, site) ::rmsb200::dbg_check((p), (bytes), (site))
+#else
+#define RMSB_DBG_OK(p, bytes, site) true
+#endif
+
+// Scalar stores / loads of the streaming and generic kernels, checked in the debug build.
+template <typename T>
+__device__ __forceinline__ void st1(T* p, T v) {
+  if (RMSB_DBG_OK(p, sizeof(T), kDbgScalarStore)) *p = v;
+}
+template <typename T>
+__device__ __forceinline__ T ld1(const T* p) {
+  return RMSB_DBG_OK(p, sizeof(T), kDbgScalarLoad) ? *p : T{};
+}
+
+// One float4 of a partial row (the dweight / dbias reductions).
+__device__ __forceinline__ float4 ld_partial4(const float* p) {
+  if (!RMSB_DBG_OK(p, 16, kDbgPartialLoad)) return make_float4(0.f, 0.f, 0.f, 0.f);
+  return *reinterpret_cast<const float4*>(p);
+}
+
 __device__ __forceinline__ bool abort_requested() {
   return *reinterpret_cast<volatile int*>(&g_status) != 0;
 }
@@ -176,6 +266,13 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
                                           uint64_t* bar, uint64_t policy) {
+#ifdef RMSB_DEBUG_BOUNDS
+  if (!RMSB_DBG_OK(gsrc, bytes, kDbgBulkSrc) || !RMSB_DBG_OK(smem_dst, bytes, kDbgBulkDst)) {
+    // the bytes the consumers wait for are completed without a copy
+    asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+    return;
+  }
+#endif
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
       "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(smem_dst)),
@@ -187,24 +284,42 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
 // warms the lines a later bulk_load of the same range will read. Source 16-byte aligned,
 // size a multiple of 16.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, uint32_t bytes) {
+  if (!RMSB_DBG_OK(gsrc, bytes, kDbgPrefetch)) return;
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
 }
 
 // Non-bulk async copy of 4 or 16 bytes; completion is attached to an mbarrier with
 // cp_async_arrive (which raises the barrier's expected arrivals by one first, so the
 // phase cannot complete before these copies land).
+// The bounds-checked build checks a run of these copies as a whole before issuing it, and
+// makes them plain synchronous copies with no arrive of their own: its out-of-line checker
+// calls, falling between async copies and their tracking arrive, left that arrive
+// undelivered on B200 (a wait that timed out). The issuing thread's copies then precede
+// its expect-tx arrive on the slot, which the consumers acquire.
 __device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gsrc) {
+#ifdef RMSB_DEBUG_BOUNDS
+  *static_cast<uint32_t*>(smem_dst) = *static_cast<const uint32_t*>(gsrc);
+#else
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
                : "memory");
+#endif
 }
 
 __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
+#ifdef RMSB_DEBUG_BOUNDS
+  *static_cast<uint4*>(smem_dst) = *static_cast<const uint4*>(gsrc);
+#else
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
                : "memory");
+#endif
 }
 
 __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+#ifdef RMSB_DEBUG_BOUNDS
+  (void)bar;  // the copies above were synchronous: the phase needs no extra arrival
+#else
   asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+#endif
 }
 
 // ---------------------------------------------------------------------------------------
@@ -255,9 +370,11 @@ __device__ __forceinline__ void st_async_peer(uint32_t remote_addr, float v, uin
 
 // Global-memory accesses of the cross-CTA exchange (gpu scope; not cached in L1).
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+  if (!RMSB_DBG_OK(p, 8, kDbgRecord)) return;
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  if (!RMSB_DBG_OK(p, 8, kDbgRecord)) return 0ull;
   unsigned long long v;
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
@@ -338,18 +455,21 @@ template <>
 struct Vec8<float> {
   static constexpr int kBytes = 32;
   __device__ __forceinline__ static void load(const void* p, float (&v)[8]) {
+    if (!RMSB_DBG_OK(p, 32, kDbgVecLoad)) { for (float& e : v) e = 0.f; return; }
     const float4 a = reinterpret_cast<const float4*>(p)[0];
     const float4 b = reinterpret_cast<const float4*>(p)[1];
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   }
   __device__ __forceinline__ static void load_global(const void* p, float (&v)[8]) {
+    if (!RMSB_DBG_OK(p, 32, kDbgVecLoad)) { for (float& e : v) e = 0.f; return; }
     const float4 a = __ldg(reinterpret_cast<const float4*>(p));
     const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   }
   __device__ __forceinline__ static void store(void* p, const float (&v)[8]) {
+    if (!RMSB_DBG_OK(p, 32, kDbgVecStore)) return;
     __stcs(reinterpret_cast<float4*>(p), make_float4(v[0], v[1], v[2], v[3]));
     __stcs(reinterpret_cast<float4*>(p) + 1, make_float4(v[4], v[5], v[6], v[7]));
   }
@@ -387,12 +507,15 @@ struct Vec8<__nv_bfloat16> {
     unpack_bf16x2(u.w, v[6], v[7]);
   }
   __device__ __forceinline__ static void load(const void* p, float (&v)[8]) {
+    if (!RMSB_DBG_OK(p, 16, kDbgVecLoad)) { for (float& e : v) e = 0.f; return; }
     unpack(*reinterpret_cast<const uint4*>(p), v);
   }
   __device__ __forceinline__ static void load_global(const void* p, float (&v)[8]) {
+    if (!RMSB_DBG_OK(p, 16, kDbgVecLoad)) { for (float& e : v) e = 0.f; return; }
     unpack(__ldg(reinterpret_cast<const uint4*>(p)), v);
   }
   __device__ __forceinline__ static void store(void* p, const float (&v)[8]) {
+    if (!RMSB_DBG_OK(p, 16, kDbgVecStore)) return;
     uint4 u;
     u.x = pack_bf16x2(v[0], v[1]);
     u.y = pack_bf16x2(v[2], v[3]);
@@ -412,12 +535,15 @@ struct Vec8<__half> {
     unpack_f16x2(u.w, v[6], v[7]);
   }
   __device__ __forceinline__ static void load(const void* p, float (&v)[8]) {
+    if (!RMSB_DBG_OK(p, 16, kDbgVecLoad)) { for (float& e : v) e = 0.f; return; }
     unpack(*reinterpret_cast<const uint4*>(p), v);
   }
   __device__ __forceinline__ static void load_global(const void* p, float (&v)[8]) {
+    if (!RMSB_DBG_OK(p, 16, kDbgVecLoad)) { for (float& e : v) e = 0.f; return; }
     unpack(__ldg(reinterpret_cast<const uint4*>(p)), v);
   }
   __device__ __forceinline__ static void store(void* p, const float (&v)[8]) {
+    if (!RMSB_DBG_OK(p, 16, kDbgVecStore)) return;
     uint4 u;
     u.x = pack_f16x2(v[0], v[1]);
     u.y = pack_f16x2(v[2], v[3]);
@@ -436,18 +562,21 @@ struct Pair8;
 template <>
 struct Pair8<float> {
   __device__ __forceinline__ static void load(const void* p, float2 (&v)[4]) {
+    if (!RMSB_DBG_OK(p, 32, kDbgVecLoad)) { for (float2& e : v) e = make_float2(0.f, 0.f); return; }
     const float4 a = reinterpret_cast<const float4*>(p)[0];
     const float4 b = reinterpret_cast<const float4*>(p)[1];
     v[0] = make_float2(a.x, a.y); v[1] = make_float2(a.z, a.w);
     v[2] = make_float2(b.x, b.y); v[3] = make_float2(b.z, b.w);
   }
   __device__ __forceinline__ static void load_global(const void* p, float2 (&v)[4]) {
+    if (!RMSB_DBG_OK(p, 32, kDbgVecLoad)) { for (float2& e : v) e = make_float2(0.f, 0.f); return; }
     const float4 a = __ldg(reinterpret_cast<const float4*>(p));
     const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
     v[0] = make_float2(a.x, a.y); v[1] = make_float2(a.z, a.w);
     v[2] = make_float2(b.x, b.y); v[3] = make_float2(b.z, b.w);
   }
   __device__ __forceinline__ static void store(void* p, const float2 (&v)[4]) {
+    if (!RMSB_DBG_OK(p, 32, kDbgVecStore)) return;
     __stcs(reinterpret_cast<float4*>(p), make_float4(v[0].x, v[0].y, v[1].x, v[1].y));
     __stcs(reinterpret_cast<float4*>(p) + 1, make_float4(v[2].x, v[2].y, v[3].x, v[3].y));
   }
@@ -478,12 +607,15 @@ struct Pair8<__nv_bfloat16> {
     v[2] = unpack_bf16x2_pair(u.z); v[3] = unpack_bf16x2_pair(u.w);
   }
   __device__ __forceinline__ static void load(const void* p, float2 (&v)[4]) {
+    if (!RMSB_DBG_OK(p, 16, kDbgVecLoad)) { for (float2& e : v) e = make_float2(0.f, 0.f); return; }
     unpack(*reinterpret_cast<const uint4*>(p), v);
   }
   __device__ __forceinline__ static void load_global(const void* p, float2 (&v)[4]) {
+    if (!RMSB_DBG_OK(p, 16, kDbgVecLoad)) { for (float2& e : v) e = make_float2(0.f, 0.f); return; }
     unpack(__ldg(reinterpret_cast<const uint4*>(p)), v);
   }
   __device__ __forceinline__ static void store(void* p, const float2 (&v)[4]) {
+    if (!RMSB_DBG_OK(p, 16, kDbgVecStore)) return;
     uint4 u;
     u.x = pack_bf16x2_pair(v[0]); u.y = pack_bf16x2_pair(v[1]);
     u.z = pack_bf16x2_pair(v[2]); u.w = pack_bf16x2_pair(v[3]);
@@ -498,12 +630,15 @@ struct Pair8<__half> {
     v[2] = unpack_f16x2_pair(u.z); v[3] = unpack_f16x2_pair(u.w);
   }
   __device__ __forceinline__ static void load(const void* p, float2 (&v)[4]) {
+    if (!RMSB_DBG_OK(p, 16, kDbgVecLoad)) { for (float2& e : v) e = make_float2(0.f, 0.f); return; }
     unpack(*reinterpret_cast<const uint4*>(p), v);
   }
   __device__ __forceinline__ static void load_global(const void* p, float2 (&v)[4]) {
+    if (!RMSB_DBG_OK(p, 16, kDbgVecLoad)) { for (float2& e : v) e = make_float2(0.f, 0.f); return; }
     unpack(__ldg(reinterpret_cast<const uint4*>(p)), v);
   }
   __device__ __forceinline__ static void store(void* p, const float2 (&v)[4]) {
+    if (!RMSB_DBG_OK(p, 16, kDbgVecStore)) return;
     uint4 u;
     u.x = pack_f16x2_pair(v[0]); u.y = pack_f16x2_pair(v[1]);
     u.z = pack_f16x2_pair(v[2]); u.w = pack_f16x2_pair(v[3]);
@@ -569,12 +704,14 @@ __device__ __forceinline__ void store8_rt(void* base, int dt, int64_t e, const f
 
 // Scalar runtime-dtype access (generic kernels).
 __device__ __forceinline__ float load1_rt(const void* base, int dt, int64_t e) {
+  if (!RMSB_DBG_OK(static_cast<const char*>(base) + e * dtype_bytes(dt), dtype_bytes(dt), kDbgScalarLoad)) return 0.f;
   if (dt == RMSNORM_B200_F32) return reinterpret_cast<const float*>(base)[e];
   if (dt == RMSNORM_B200_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[e]);
   return __half2float(reinterpret_cast<const __half*>(base)[e]);
 }
 
 __device__ __forceinline__ void store1_rt(void* base, int dt, int64_t e, float v) {
+  if (!RMSB_DBG_OK(static_cast<char*>(base) + e * dtype_bytes(dt), dtype_bytes(dt), kDbgScalarStore)) return;
   if (dt == RMSNORM_B200_F32) {
     reinterpret_cast<float*>(base)[e] = v;
   } else if (dt == RMSNORM_B200_BF16) {

@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(kGenericThreads) fwd_generic_kernel(const GenF
       const float b = p.b ? load1_rt(p.b, p.b_dt, (p.b_ph ? head * N : 0) + n) : 0.f;
       store1_rt(p.out, p.out_dt, base + n, fmaf(v * rs, w, b));
     }
-    if (threadIdx.x == 0 && p.rstd) p.rstd[r] = rs;
+    if (threadIdx.x == 0 && p.rstd) st1(&p.rstd[r], rs);
   }
 }
 
@@ -113,8 +113,8 @@ __global__ void __launch_bounds__(kGenericThreads) ln_generic_kernel(const GenLn
       }
     }
     if (threadIdx.x == 0) {
-      if (p.mean) p.mean[r] = mean;
-      if (p.rstd) p.rstd[r] = rs;
+      if (p.mean) st1(&p.mean[r], mean);
+      if (p.rstd) st1(&p.rstd[r], rs);
     }
   }
 }
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(kGenericThreads) bwd_generic_dx_kernel(const G
   for (int64_t r = blockIdx.x; r < p.rows; r += gridDim.x) {
     const int64_t base = r * N;
     const int64_t woff = p.w_ph ? (r % p.H) * N : 0;
-    const float rs = p.rstd[r];
+    const float rs = ld1(&p.rstd[r]);
     float acc = 0.f;
     for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
       const float xh = load1_rt(p.x, p.x_dt, base + n) * rs;
@@ -160,12 +160,12 @@ __global__ void __launch_bounds__(kGenericThreads) bwd_generic_partials_kernel(
   for (int64_t t = t0; t < t1; ++t) {
     const int64_t e = t * W + j;
     const float dy = load1_rt(p.dy, p.dy_dt, e);
-    const float xh = load1_rt(p.x, p.x_dt, e) * p.rstd[t * p.H + head];
+    const float xh = load1_rt(p.x, p.x_dt, e) * ld1(&p.rstd[t * p.H + head]);
     dw = fmaf(dy, xh, dw);
     db += dy;
   }
-  if (dw_part) dw_part[static_cast<int64_t>(blockIdx.y) * W + j] = dw;
-  if (db_part) db_part[static_cast<int64_t>(blockIdx.y) * W + j] = db;
+  if (dw_part) st1(&dw_part[static_cast<int64_t>(blockIdx.y) * W + j], dw);
+  if (db_part) st1(&db_part[static_cast<int64_t>(blockIdx.y) * W + j], db);
 }
 
 // out[j] = sum over partial rows c < C and heads h < fold of part[c][h * N + j], in a fixed
@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_partials_kernel(const R
 #pragma unroll
         for (int u = 0; u < kReduceBatch; ++u) {
           const int64_t c = c0 + u * kReduceWarps;
-          v[u] = c < p.C ? *reinterpret_cast<const float4*>(col + c * p.W) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[u] = c < p.C ? ld_partial4(col + c * p.W) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int u = 0; u < kReduceBatch; ++u) {
@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_partials_kernel(const R
       for (; c + (kReduceUnroll - 1) * kReduceWarps < p.C; c += kReduceUnroll * kReduceWarps) {
         float v[kReduceUnroll];
 #pragma unroll
-        for (int u = 0; u < kReduceUnroll; ++u) v[u] = col[(c + u * kReduceWarps) * p.W];
+        for (int u = 0; u < kReduceUnroll; ++u) v[u] = ld1(&col[(c + u * kReduceWarps) * p.W]);
 #pragma unroll
         for (int u = 0; u < kReduceUnroll; ++u) acc += v[u];
       }
@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_partials_kernel(const R
       for (; c < p.C; c += kReduceWarps) {
         const float* row = col + c * p.W;
         float t = 0.f;
-        for (int h = 0; h < jb.fold; ++h) t += row[h * p.N];
+        for (int h = 0; h < jb.fold; ++h) t += ld1(&row[h * p.N]);
         acc += t;
       }
     }

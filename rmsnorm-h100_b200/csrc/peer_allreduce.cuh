@@ -48,9 +48,11 @@ struct PeerParams {
 };
 
 __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  if (!RMSB_DBG_OK(p, 8, kDbgPeerWord)) return;
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  if (!RMSB_DBG_OK(p, 8, kDbgPeerWord)) return 0ull;
   unsigned long long v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
@@ -90,7 +92,7 @@ __global__ void __launch_bounds__(kARThreads, 1) reduce_allreduce_kernel(const R
 #pragma unroll
           for (int u = 0; u < kARUnroll; ++u) {
             const int64_t c = c0 + u * kARWarps;
-            v[u] = c < rp.C ? *reinterpret_cast<const float4*>(col + c * rp.W) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[u] = c < rp.C ? ld_partial4(col + c * rp.W) : make_float4(0.f, 0.f, 0.f, 0.f);
           }
 #pragma unroll
           for (int u = 0; u < kARUnroll; ++u) {
@@ -110,10 +112,10 @@ __global__ void __launch_bounds__(kARThreads, 1) reduce_allreduce_kernel(const R
           for (int64_t c = warp; c < rp.C; c += kARWarps) {
             const float* row = jb.part + c * rp.W + j;
             if (jb.fold == 1) {
-              t += row[0];
+              t += ld1(&row[0]);
             } else {
               float f = 0.f;
-              for (int h = 0; h < jb.fold; ++h) f += row[h * rp.N];
+              for (int h = 0; h < jb.fold; ++h) f += ld1(&row[h * rp.N]);
               t += f;
             }
           }

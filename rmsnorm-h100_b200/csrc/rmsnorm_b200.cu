@@ -439,6 +439,38 @@ std::string describe(const char* kind, const StreamPlan& pl, int grid) {
   return buf;
 }
 
+#ifdef RMSB_DEBUG_BOUNDS
+// Bounds-checked build: the byte ranges the kernels of one API call may access, written to
+// the device (dbg_ranges_kernel) on the call's stream before its first launch. The
+// internal record arrays of the split-row exchange are always included.
+struct DbgList {
+  DbgRanges r{};
+  void add(const void* p, size_t bytes) {
+    if (!p || bytes == 0 || r.n >= kDbgMaxRanges) return;
+    r.lo[r.n] = reinterpret_cast<uintptr_t>(p);
+    r.hi[r.n] = r.lo[r.n] + bytes;
+    ++r.n;
+  }
+};
+
+int dbg_register(DbgList& l, cudaStream_t stream) {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_xrec) == cudaSuccess) l.add(p, sizeof(g_xrec));
+  if (cudaGetSymbolAddress(&p, g_xgen) == cudaSuccess) l.add(p, sizeof(g_xgen));
+  cudaGetLastError();
+  dbg_ranges_kernel<<<1, 32, 0, stream>>>(l.r);
+  return cudaGetLastError() == cudaSuccess ? RMSNORM_B200_OK : RMSNORM_B200_ERR_CUDA;
+}
+
+// Self test of the checker: RMSNORM_B200_DEBUG_CLIP_OUT=k registers the output tensor of a
+// forward k bytes short, so the kernel's (in-bounds) stores to its last k bytes are
+// reported and skipped.
+size_t dbg_clip(size_t bytes) {
+  const int c = env_int("RMSNORM_B200_DEBUG_CLIP_OUT", 0);
+  return c > 0 && static_cast<size_t>(c) < bytes ? bytes - static_cast<size_t>(c) : bytes;
+}
+#endif
+
 // Sizes the grid (persistent: as many clusters or groups as can be resident, at most one
 // per tile), picks the row-total exchange for split rows and, unless dry_run, launches.
 // Clusters of 4, 8 or 16 CTAs fit fewer times on the GPU than the SM count allows (on
@@ -759,6 +791,22 @@ int do_fwd(const rmsnorm_b200_fwd_args* a, cudaStream_t stream) {
   DeviceState* ds = nullptr;
   st = get_device_state(&ds);
   if (st) return st;
+#ifdef RMSB_DEBUG_BOUNDS
+  {
+    DbgList l;
+    const size_t n = static_cast<size_t>(a->rows) * static_cast<size_t>(a->hidden);
+    const size_t hd = static_cast<size_t>(a->hidden);
+    l.add(a->x, n * elem_bytes(a->x_dtype));
+    if (a->residual) l.add(a->residual, n * elem_bytes(a->residual_dtype));
+    if (a->weight) l.add(a->weight, std::max(a->weight_heads, 1) * hd * elem_bytes(a->weight_dtype));
+    if (a->bias) l.add(a->bias, std::max(a->bias_heads, 1) * hd * elem_bytes(a->bias_dtype));
+    l.add(a->out, dbg_clip(n * elem_bytes(a->out_dtype)));
+    if (a->residual_out) l.add(a->residual_out, n * elem_bytes(a->residual_out_dtype));
+    if (a->rstd) l.add(a->rstd, static_cast<size_t>(a->rows) * 4);
+    st = dbg_register(l, stream);
+    if (st) return st;
+  }
+#endif
   std::string why;
   FwdKernel kernel = nullptr;
   if (env_int("RMSNORM_B200_FORCE_GENERIC", 0)) {
@@ -842,6 +890,20 @@ int do_ln(const rmsnorm_b200_ln_fwd_args* a, cudaStream_t stream) {
   DeviceState* ds = nullptr;
   st = get_device_state(&ds);
   if (st) return st;
+#ifdef RMSB_DEBUG_BOUNDS
+  {
+    DbgList l;
+    const size_t n = static_cast<size_t>(a->rows) * static_cast<size_t>(a->hidden);
+    l.add(a->x, n * elem_bytes(a->x_dtype));
+    if (a->weight) l.add(a->weight, static_cast<size_t>(a->hidden) * elem_bytes(a->weight_dtype));
+    if (a->bias) l.add(a->bias, static_cast<size_t>(a->hidden) * elem_bytes(a->bias_dtype));
+    if (a->out) l.add(a->out, dbg_clip(n * elem_bytes(a->out_dtype)));
+    if (a->mean) l.add(a->mean, static_cast<size_t>(a->rows) * 4);
+    if (a->rstd) l.add(a->rstd, static_cast<size_t>(a->rows) * 4);
+    st = dbg_register(l, stream);
+    if (st) return st;
+  }
+#endif
   std::string why;
   FwdKernel kernel = nullptr;
   if (env_int("RMSNORM_B200_FORCE_GENERIC", 0)) {
@@ -1051,6 +1113,28 @@ int do_bwd(const rmsnorm_b200_bwd_args* a, void* ws, size_t ws_bytes, cudaStream
   if (st) return st;
   const size_t need = workspace_for(bp);
   if (need > ws_bytes || (need > 0 && (!ws || !aligned16(ws)))) return RMSNORM_B200_ERR_WORKSPACE;
+#ifdef RMSB_DEBUG_BOUNDS
+  {
+    DbgList l;
+    const size_t n = static_cast<size_t>(a->rows) * static_cast<size_t>(a->hidden);
+    const size_t hd = static_cast<size_t>(a->hidden);
+    l.add(a->x, n * elem_bytes(a->x_dtype));
+    l.add(a->dout, n * elem_bytes(a->dout_dtype));
+    l.add(a->rstd, static_cast<size_t>(a->rows) * 4);
+    if (a->weight) l.add(a->weight, std::max(a->weight_heads, 1) * hd * elem_bytes(a->weight_dtype));
+    if (a->dresidual_out) l.add(a->dresidual_out, n * elem_bytes(a->dresidual_out_dtype));
+    l.add(a->dx, n * elem_bytes(a->dx_dtype));
+    if (a->dresidual) l.add(a->dresidual, n * elem_bytes(a->dresidual_dtype));
+    if (a->dweight) l.add(a->dweight, std::max(a->weight_heads, 1) * hd * elem_bytes(a->dweight_dtype));
+    if (a->dbias) l.add(a->dbias, std::max(a->dbias_heads, 1) * hd * elem_bytes(a->dbias_dtype));
+    l.add(ws, ws_bytes);
+    if (group)
+      for (int q = 0; q < group->world; ++q)
+        l.add(group->recv[q], 2ull * static_cast<size_t>(group->world) * static_cast<size_t>(group->max_floats) * 8ull);
+    st = dbg_register(l, stream);
+    if (st) return st;
+  }
+#endif
   float* dw_part = bp.need_dw ? static_cast<float*>(ws) : nullptr;
   float* db_part = bp.need_db ? static_cast<float*>(ws) + (bp.need_dw ? bp.nparts * bp.W : 0) : nullptr;
 
@@ -1354,6 +1438,35 @@ extern "C" int rmsnorm_b200_max_active_clusters(int32_t cluster_size, int32_t* c
 }
 
 extern "C" int rmsnorm_b200_abi_version(void) { return RMSNORM_B200_ABI_VERSION; }
+
+extern "C" int rmsnorm_b200_debug_bounds_build(void) {
+#ifdef RMSB_DEBUG_BOUNDS
+  return 1;
+#else
+  return 0;
+#endif
+}
+
+extern "C" int rmsnorm_b200_debug_report(void* stream, uint64_t* violations, int32_t* site, uint64_t* address,
+                                         uint32_t* bytes, int32_t clear) {
+#ifdef RMSB_DEBUG_BOUNDS
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+  unsigned long long rep[4] = {0, 0, 0, 0};
+  if (cudaMemcpyFromSymbol(rep, g_dbg_report, sizeof(rep)) != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+  if (violations) *violations = rep[0];
+  if (site) *site = static_cast<int32_t>(rep[1]);
+  if (address) *address = rep[2];
+  if (bytes) *bytes = static_cast<uint32_t>(rep[3]);
+  if (clear) {
+    const unsigned long long z[4] = {0, 0, 0, 0};
+    if (cudaMemcpyToSymbol(g_dbg_report, z, sizeof(z)) != cudaSuccess) return RMSNORM_B200_ERR_CUDA;
+  }
+  return RMSNORM_B200_OK;
+#else
+  (void)stream; (void)violations; (void)site; (void)address; (void)bytes; (void)clear;
+  return RMSNORM_B200_ERR_UNSUPPORTED;
+#endif
+}
 
 extern "C" uint64_t rmsnorm_b200_launch_count(void) { return g_launches.load(); }
 

@@ -52,9 +52,8 @@ constexpr int kMaxLag = 3;  // deepest exchange lag the slots allow: kXSlots >= 
 
 constexpr int kGroupRed = 4;  // split-phase reductions per row group: 2 statistics x 2 rows in flight
 
-// Dynamic shared memory (every extern __shared__ array aliases its start): the S ring
+// Dynamic shared memory (rmsb_dyn_smem, declared with the device helpers): the S ring
 // stages, then the barrier / reduction area laid out by carve_smem.
-extern __shared__ __align__(128) unsigned char rmsb_dyn_smem[];
 
 // Byte offset, within the area after the stages, of the global-memory exchange's tag base
 // (after full, xbar, xpart, red, done, gbar and gpart).
@@ -762,14 +761,13 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
 #pragma unroll
                 for (int k = 1; k < kVecs; ++k)
                   if (i == k) v = rstd_k[k];
-                p.rstd[(row0 + lr0 + (i / kCols) * pl.rps) * pl.heads + ((gl + (i % kCols) * G) >> pl.vs_shift)] = v;
+                st1(&p.rstd[(row0 + lr0 + (i / kCols) * pl.rps) * pl.heads + ((gl + (i % kCols) * G) >> pl.vs_shift)], v);
               }
             } else if (i == 0) {
 #pragma unroll
               for (int k = 0; k < kVecs; ++k)
                 if ((ok >> k) & 1u)
-                  p.rstd[(row0 + lr0 + (k / kCols) * pl.rps) * pl.heads + ((gl + (k % kCols) * G) >> pl.vs_shift)] =
-                      rstd_k[k];
+                  st1(&p.rstd[(row0 + lr0 + (k / kCols) * pl.rps) * pl.heads + ((gl + (k % kCols) * G) >> pl.vs_shift)], rstd_k[k]);
             }
           }
         }
@@ -851,8 +849,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
 #pragma unroll
           for (int k = 0; k < kVecs; ++k) ln_emit(xs_p + k * G8, op + k * G8, m, rstd, k);
           if (gl == 0) {
-            if (p.rstd != nullptr) p.rstd[row_p] = rstd;
-            if (p.mean != nullptr) p.mean[row_p] = m;
+            if (p.rstd != nullptr) st1(&p.rstd[row_p], rstd);
+            if (p.mean != nullptr) st1(&p.mean[row_p], m);
           }
         }
         if (release_slot(L, sp, nwarps) && q - 1 + S < n_local) issue_unit(q - 1 + S, sp);
@@ -905,8 +903,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
           for (int k = 0; k < kVecs; ++k)
             if ((vmask >> k) & 1u) ln_emit(xs_p + k * G8, op + k * G8, mean_p, rstd, k);
           if (gl == 0) {
-            if (p.rstd != nullptr) p.rstd[row_p] = rstd;
-            if (p.mean != nullptr) p.mean[row_p] = mean_p;
+            if (p.rstd != nullptr) st1(&p.rstd[row_p], rstd);
+            if (p.mean != nullptr) st1(&p.mean[row_p], mean_p);
           }
         }
         if (release_slot(L, sp, nwarps) && q - 1 + S < n_local) issue_unit(q - 1 + S, sp);
@@ -967,7 +965,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
 #pragma unroll
           for (int k = 0; k < kVecs; ++k) rstd_k[k] = r;
           pass2(xs_p, rs_p, row_p, rstd_k);
-          if (p.rstd != nullptr && gl == 0) p.rstd[row_p] = r;
+          if (p.rstd != nullptr && gl == 0) st1(&p.rstd[row_p], r);
         }
         if (release_slot(L, sp, nwarps) && q - 1 + S < n_local) issue_unit(q - 1 + S, sp);
       }
@@ -1122,7 +1120,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
 #pragma unroll
           for (int k = 0; k < kVecs; ++k) rstd_k[k] = rs;
           if (in_group) pass2(stage_x(s2), stage_r(s2), row, rstd_k);
-          if (p.rstd != nullptr && tid == 0 && rank == 0) p.rstd[row] = rs;
+          if (p.rstd != nullptr && tid == 0 && rank == 0) st1(&p.rstd[row], rs);
           if (release_slot(L, s2, nwarps) && r2 + S < n_local) issue_unit(r2 + S, s2);
           if (++s2 == S) s2 = 0;
         }
@@ -1169,7 +1167,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
           if (K == 1) pass2(stage_x(s2), stage_r(s2), row, rstd_k);
           else pass2c(s2, row, rs);
         }
-        if (p.rstd != nullptr && tid == 0 && rank == 0) p.rstd[row] = rs;
+        if (p.rstd != nullptr && tid == 0 && rank == 0) st1(&p.rstd[row], rs);
         if (K == 1) {
           if (release_slot(L, s2, nwarps) && r2 + S < n_local)
             issue_unit(r2 + S, s2);
@@ -1218,10 +1216,13 @@ __device__ __forceinline__ void bwd_issue(const BwdParams& p, const StreamPlan& 
   const uint32_t rbytes = static_cast<uint32_t>(cnt) * 4u;
   const bool rbulk = kRstdBulk && (reinterpret_cast<uintptr_t>(rsrc) & 15u) == 0 && (rbytes & 15u) == 0;
   if (!rbulk) {
-    int c = 0;
-    if ((reinterpret_cast<uintptr_t>(rsrc) & 15u) == 0)
-      for (; c + 4 <= cnt; c += 4) cp_async_16(rdst + c, rsrc + c);
-    for (; c < cnt; ++c) cp_async_4(rdst + c, rsrc + c);
+    // the bounds-checked build checks the whole run once, before the first copy
+    if (RMSB_DBG_OK(rsrc, rbytes, kDbgAsyncCopy) && RMSB_DBG_OK(rdst, rbytes, kDbgAsyncCopy)) {
+      int c = 0;
+      if ((reinterpret_cast<uintptr_t>(rsrc) & 15u) == 0)
+        for (; c + 4 <= cnt; c += 4) cp_async_16(rdst + c, rsrc + c);
+      for (; c < cnt; ++c) cp_async_4(rdst + c, rsrc + c);
+    }
     cp_async_arrive(&L.full[s]);
   }
   const uint32_t b0 = static_cast<uint32_t>(rows) * pl.row_bytes[0];
@@ -1452,7 +1453,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
   auto pass1 = [&](const RowPtrs& rp, float (&part)[kVecs], float (&rstd_k)[kVecs]) {
     if constexpr (kTmemAcc) {
       tmem_wait_st();  // the previous row's sums are in TMEM before they are read again
-      const float r = rp.rstd[0];  // row mode: one rstd per row
+      const float r = ld1(&rp.rstd[0]);  // row mode: one rstd per row
 #pragma unroll
       for (int k = 0; k < kVecs; ++k) {
         rstd_k[k] = r;
@@ -1465,7 +1466,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
       part[k] = 0.f;
       rstd_k[k] = 0.f;
       if ((vmask >> k) & 1u) {
-        const float r = rp.rstd[pl.seg_mode ? ((gl + k * G) >> pl.vs_shift) : 0];
+        const float r = ld1(&rp.rstd[pl.seg_mode ? ((gl + k * G) >> pl.vs_shift) : 0]);
         rstd_k[k] = r;
         part[k] = dot_acc(rp.x + k * G8, rp.dy + k * G8, r, k);
       }
@@ -1550,8 +1551,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
             part[k] = 0.f;
             rstd_k[k] = 0.f;
             if ((ok >> k) & 1u) {
-              const float r = rp.rstd[(lr0 + (k / kCols) * pl.rps) * rstd_per_row +
-                                      ((gl + (k % kCols) * G) >> pl.vs_shift)];
+              const float r = ld1(&rp.rstd[(lr0 + (k / kCols) * pl.rps) * rstd_per_row +
+                                      ((gl + (k % kCols) * G) >> pl.vs_shift)]);
               rstd_k[k] = r;
               part[k] = dot_acc(rp.x + eoff(k), rp.dy + eoff(k), r, k);
             }
@@ -1596,7 +1597,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
           const RowPtrs rp = row_ptrs(s, gid);
           float part[kVecs], rstd_k[kVecs];
           pass1(rp, part, rstd_k);
-          rstd_q = rp.rstd[0];
+          rstd_q = ld1(&rp.rstd[0]);
 #pragma unroll
           for (int k = 0; k < kVecs; ++k) dot += part[k];
         }
@@ -1692,10 +1693,10 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
           if (K == 1) {
             float rstd_k[kVecs], c_k[kVecs];
 #pragma unroll
-            for (int k = 0; k < kVecs; ++k) { rstd_k[k] = rp.rstd[0]; c_k[k] = c; }
+            for (int k = 0; k < kVecs; ++k) { rstd_k[k] = ld1(&rp.rstd[0]); c_k[k] = c; }
             pass2(rp, row, rstd_k, c_k);
           } else {
-            pass2c(s2, row, rp.rstd[0], c);
+            pass2c(s2, row, ld1(&rp.rstd[0]), c);
           }
         }
         for (int j = 0; j < K; ++j) {

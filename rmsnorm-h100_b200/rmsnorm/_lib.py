@@ -128,6 +128,12 @@ SIGNATURES = {
     "rmsnorm_b200_abi_version": (ctypes.c_int, []),
     "rmsnorm_b200_max_active_clusters": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]),
     "rmsnorm_b200_launch_count": (ctypes.c_uint64, []),
+    "rmsnorm_b200_debug_bounds_build": (ctypes.c_int, []),
+    "rmsnorm_b200_debug_report": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_int32),
+         ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32],
+    ),
     "rmsnorm_b200_peer_buffer_size": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int64, ctypes.POINTER(ctypes.c_size_t)]),
     "rmsnorm_b200_peer_group_create": (
         ctypes.c_int,
@@ -444,6 +450,28 @@ def max_active_clusters(device: torch.device, cluster_size: int) -> int:
 
 def launch_count() -> int:
     return int(load_library().rmsnorm_b200_launch_count())
+
+
+def debug_bounds_build() -> bool:
+    """True for the bounds-checked build (librmsnorm_b200_debug.so)."""
+    return bool(load_library().rmsnorm_b200_debug_bounds_build())
+
+
+def debug_report(device: torch.device, clear: bool = False) -> dict:
+    """Failed bounds checks since the last clear (bounds-checked build only): count and the
+    first one's site code, address and size. Synchronises the current stream."""
+    lib = load_library()
+    n = ctypes.c_uint64(0)
+    site = ctypes.c_int32(0)
+    addr = ctypes.c_uint64(0)
+    nbytes = ctypes.c_uint32(0)
+    with torch.cuda.device(device):
+        _check(
+            lib.rmsnorm_b200_debug_report(_stream_handle(device), ctypes.byref(n), ctypes.byref(site),
+                                          ctypes.byref(addr), ctypes.byref(nbytes), int(clear)),
+            "rmsnorm_b200_debug_report",
+        )
+    return {"violations": int(n.value), "site": int(site.value), "address": int(addr.value), "bytes": int(nbytes.value)}
 
 
 def last_plan() -> str:

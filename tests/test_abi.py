@@ -33,6 +33,21 @@ def test_library_exports_every_declared_symbol():
     assert lib.rmsnorm_b200_abi_version() == _lib.ABI_VERSION
 
 
+def test_release_and_bounds_checked_builds_identify_themselves():
+    """Both builds export the same symbols; only the bounds-checked one says so and keeps
+    a report (the release build answers UNSUPPORTED without touching a device)."""
+    lib = _lib.load_library()
+    assert lib.rmsnorm_b200_debug_bounds_build() == 0
+    assert lib.rmsnorm_b200_debug_report(None, None, None, None, None, 0) == 2  # UNSUPPORTED
+    debug_path = Path(_lib.__file__).resolve().parent / "lib" / "librmsnorm_b200_debug.so"
+    if not debug_path.exists():
+        pytest.skip("bounds-checked build not built (__graft_entry__.build() makes it)")
+    dbg = ctypes.CDLL(str(debug_path))
+    for name in _declared_functions():
+        assert hasattr(dbg, name), f"{name} not exported by the bounds-checked build"
+    assert dbg.rmsnorm_b200_debug_bounds_build() == 1
+
+
 def _c_layout(struct_name, fields):
     src = ["#include <stddef.h>", "#include <stdio.h>", f'#include "{HEADER}"', "int main(void) {",
            f'  printf("%zu\\n", sizeof({struct_name}));']
