@@ -261,11 +261,21 @@ __device__ __forceinline__ void cluster_send(float v, const StreamPlan& pl, cons
     st_async_peer(map_peer(smem_u32(&xp[rank]), lane), v, map_peer(smem_u32(&L.xbar[slot]), lane));
 }
 
-// `pre`: this lane's xrec_load for the row (kXGlobal).
-__device__ __forceinline__ float cluster_recv(const StreamPlan& pl, const SmemLayout& L, const XCtx& xc, int lane,
-                                              uint32_t seq, XRecord pre, int site) {
+// `pre`: this lane's xrec_load for the row (kXGlobal). With pl.xbcast, warp 0 alone polls
+// the records and posts the total into the slot's xpart word, arriving on its xbar (both
+// otherwise unused by the global exchange); the other warps wait there. The slot's k-th use
+// completes phase k; the CTA-wide row sum before every exchange keeps the warps within a
+// row of each other, so no warp is a whole slot cycle (8 rows) behind.
+// kBcast = false compiles the broadcast out (kernels the planner never gives pl.xbcast).
+template <bool kBcast = true>
+__device__ __forceinline__ float cluster_recv(const StreamPlan& pl, const SmemLayout& L, const XCtx& xc, int warp,
+                                              int lane, uint32_t seq, XRecord pre, int site) {
   const uint32_t slot = seq & (kXSlots - 1);
   if (pl.xmode == kXGlobal) {
+    if (kBcast && pl.xbcast && warp != 0) {
+      mbar_wait(&L.xbar[slot], (seq / kXSlots) & 1u, site);
+      return L.xpart[slot * kMaxCluster];
+    }
     const uint32_t want = xrec_tag(pl, seq);
     XRecord w = pre;
     uint64_t t0 = 0;
@@ -281,7 +291,12 @@ __device__ __forceinline__ float cluster_recv(const StreamPlan& pl, const SmemLa
       __nanosleep(20);
       w = xrec_load(pl, xc, lane, seq);
     }
-    return warp_sum(lane < pl.P ? __uint_as_float(static_cast<uint32_t>(w)) : 0.f);
+    const float tot = warp_sum(lane < pl.P ? __uint_as_float(static_cast<uint32_t>(w)) : 0.f);
+    if (kBcast && pl.xbcast && lane == 0) {
+      L.xpart[slot * kMaxCluster] = tot;
+      mbar_arrive(&L.xbar[slot]);
+    }
+    return tot;
   }
   mbar_wait<true>(&L.xbar[slot], (seq / kXSlots) & 1u, site);
   const float* xp = L.xpart + slot * kMaxCluster;
@@ -328,8 +343,8 @@ __device__ __forceinline__ void cluster_recv2(const StreamPlan& pl, const SmemLa
     tb = __shfl_sync(0xffffffffu, v, 16);
     return;
   }
-  ta = cluster_recv(pl, L, xc, lane, seq_a, 0ull, site);
-  tb = hb ? cluster_recv(pl, L, xc, lane, seq_a + 1, 0ull, site) : 0.f;
+  ta = cluster_recv<false>(pl, L, xc, 0, lane, seq_a, 0ull, site);  // cluster exchange
+  tb = hb ? cluster_recv<false>(pl, L, xc, 0, lane, seq_a + 1, 0ull, site) : 0.f;
 }
 
 // Two rows' CTA-wide sums behind one barrier (split rows: one row group, gid 0). `buf`
@@ -1134,7 +1149,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
     uint32_t ph1 = 0;
     for (int64_t i = 0; i < n_local + lag; ++i) {
       const int64_t r2 = i - lag;
-      const XRecord pre = r2 >= 0 ? xrec_load(pl, xc, lane, static_cast<uint32_t>(r2)) : 0ull;
+      const XRecord pre =
+          r2 >= 0 && (!pl.xbcast || warp == 0) ? xrec_load(pl, xc, lane, static_cast<uint32_t>(r2)) : 0ull;
       if (i < n_local) {
         float part[kVecs];
         if (K == 1) {
@@ -1157,7 +1173,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
         if (s1 >= S) { s1 -= S; ph1 ^= 1u; }
       }
       if (r2 >= 0 && r2 < n_local) {
-        const float tot = cluster_recv(pl, L, xc, lane, static_cast<uint32_t>(r2), pre, kSiteFwdCluster);
+        const float tot =
+            cluster_recv<!kRes && !kRO>(pl, L, xc, warp, lane, static_cast<uint32_t>(r2), pre, kSiteFwdCluster);
         const int64_t row = cid + r2 * ncl;
         float rstd_k[kVecs];
         const float rs = rsqrtf(fmaf(tot, inv_n, p.eps));
@@ -1662,7 +1679,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
     uint32_t ph1 = 0;
     for (int64_t i = 0; i < n_local + lag; ++i) {
       const int64_t r2 = i - lag;
-      const XRecord pre = r2 >= 0 ? xrec_load(pl, xc, lane, static_cast<uint32_t>(r2)) : 0ull;
+      const XRecord pre =
+          r2 >= 0 && (!pl.xbcast || warp == 0) ? xrec_load(pl, xc, lane, static_cast<uint32_t>(r2)) : 0ull;
       if (i < n_local) {
         float part[kVecs];
         if (K == 1) {
@@ -1686,7 +1704,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) bwd_stream_kernel(const Bw
         if (s1 >= S) { s1 -= S; ph1 ^= 1u; }
       }
       if (r2 >= 0 && r2 < n_local) {
-        const float c = cluster_recv(pl, L, xc, lane, static_cast<uint32_t>(r2), pre, kSiteBwdCluster) * inv_n;
+        const float c = cluster_recv(pl, L, xc, warp, lane, static_cast<uint32_t>(r2), pre, kSiteBwdCluster) * inv_n;
         const int64_t row = cid + r2 * ncl;
         const RowPtrs rp = row_ptrs(s2, 0);
         if (in_group) {

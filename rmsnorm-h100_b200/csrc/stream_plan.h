@@ -37,6 +37,8 @@ struct StreamPlan {
   int32_t xmode;      // P > 1: kXCluster (DSMEM exchange) or kXGlobal (global-memory records)
   int32_t pf;         // ring units between a refill and the L2 prefetch issued with it (0 = none)
   int32_t pipe_rows;  // RMSNorm row mode: rows pipelined one tile deep (ring holds one more slot)
+  int32_t xbcast;     // kXGlobal: warp 0 alone polls the records and posts the row total to
+                      // the other warps (xpart / xbar of the row's slot)
   int32_t lag;        // rows the cluster exchange lags pass 1 by (P > 1): pass 2 of row i-lag
                       // follows pass 1 of row i
   int32_t xpair;      // forward split rows: rows go in pairs (one CTA-wide sum, one exchange

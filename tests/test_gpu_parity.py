@@ -596,6 +596,39 @@ def test_split_row_pairs_match_row_by_row(monkeypatch, xmode, rows, n, dtype):
     assert _lib.device_status(DEV) == (0, 0)
 
 
+@pytest.mark.parametrize("rows,n,dtype", [(37, 262144, BF16), (300, 65536, F16), (3, 131072, BF16)])
+def test_split_row_record_poll_by_one_warp_matches_all_warps(monkeypatch, rows, n, dtype):
+    """Global-record exchange with warp 0 alone polling and posting the row total to the
+    other warps through shared memory (the default for row slices of at most 32 KB) gives the
+    same bits as every warp polling, forward and backward, and matches the oracle."""
+    monkeypatch.setenv("RMSNORM_B200_XMODE", "1")
+    x = _g((rows, n), dtype, 500 + rows)
+    dy = _g((rows, n), dtype, 501 + rows)
+    w = _g((n,), F32, 502, "weight")
+
+    def run():
+        out, _, rstd = rmsnorm.rmsnorm_fwd(x, w, None, None, store_rstd=True)
+        torch.cuda.synchronize()
+        pf = _lib.last_plan()
+        dx, dw, _, _ = rmsnorm.rmsnorm_bwd(x, w, dy, rstd)
+        torch.cuda.synchronize()
+        return (out, rstd, dx, dw), pf, _lib.last_plan()
+
+    one, pf1, pb1 = run()
+    assert "bcast" in pf1 and "bcast" in pb1, (pf1, pb1)
+    monkeypatch.setenv("RMSNORM_B200_XBCAST", "0")
+    every, pf0, pb0 = run()
+    assert "bcast" not in pf0 and "bcast" not in pb0, (pf0, pb0)
+    for a, b in zip(one, every):
+        assert torch.equal(a, b), (pf1, pb1)
+    idx = torch.arange(0, rows, max(1, rows // 8))
+    _, _, o_rstd, y = oracle.fwd(x[idx].cpu(), w.cpu())
+    oracle.check_close(one[0][idx], y, dtype, f"out [{pf1}]")
+    o_dx, _, _, _, _ = oracle.bwd(x[idx].cpu(), w.cpu(), dy[idx].cpu(), one[1][idx].cpu())
+    oracle.check_close(one[2][idx], o_dx, dtype, f"dx [{pb1}]")
+    assert _lib.device_status(DEV) == (0, 0)
+
+
 def test_split_row_global_exchange_concurrent_streams(monkeypatch):
     """Two split-row launches with the global-memory exchange running at the same time on
     two streams (launch epochs pick different record sets) give the same bits as the same
