@@ -855,13 +855,13 @@ int do_fwd(const rmsnorm_b200_fwd_args* a, cudaStream_t stream) {
       planned = make_stream_plan(a->rows, a->hidden, a->heads, in_bytes, false, kMaxVecs, kLarge,
                                  env_int("RMSNORM_B200_FORCE_CLUSTER", 0), &pl, &why);
     if (planned) {
-      // Split rows over 2 or 4 CTAs whose ring holds two pairs of row slices and two more
-      // loading go in pairs. Measured on B200 (bf16, CUDA-graph replays, interleaved A/B):
-      // P = 2 +11.6 %, P = 4 +5 %, but P = 8 -6.7 % and P = 16 -6 %, where each pair's
-      // exchange waits on the records of twice as many CTAs.
-      if (pl.P > 1 && pl.K == 1 && pl.P <= 4 && pl.S >= 6 && !a->residual && !a->residual_out &&
-          env_int("RMSNORM_B200_XPAIR", 1) &&
-          env_int("RMSNORM_B200_FORCE_LAG", -1) < 0) {
+      // Split rows whose ring holds two pairs of row slices and two more loading go in pairs
+      // (residual-free forwards). Measured on B200 (bf16, CUDA-graph replays, two repeats,
+      // bitwise equal to the row loop): P = 16 +21 % (cfg 5: 4550 -> 5510 GB/s), P = 8 +21 %,
+      // P = 4 +21 %, P = 2 +14 %. Before warp 0 alone polled the global records, pairs lost at
+      // P = 8 and 16 (every warp polled twice as many records per exchange).
+      if (pl.P > 1 && pl.K == 1 && pl.P <= 16 && pl.S >= 6 && !a->residual && !a->residual_out &&
+          env_int("RMSNORM_B200_XPAIR", 1) && env_int("RMSNORM_B200_FORCE_LAG", -1) < 0) {
         pl.xpair = 1;
         pl.lag = 1;
       }

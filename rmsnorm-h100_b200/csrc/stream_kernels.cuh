@@ -317,9 +317,23 @@ __device__ __forceinline__ XRecord xrec_load2(const StreamPlan& pl, const XCtx& 
 // row's P values in lanes 0..P-1 adds zeros at its first level (offset 16) and then runs
 // offsets 8..1 over the 16 lanes, so the 16-lane sums here give the same bits as
 // cluster_recv. Cluster exchange: the two rows one after the other.
-__device__ __forceinline__ void cluster_recv2(const StreamPlan& pl, const SmemLayout& L, const XCtx& xc, int lane,
-                                              uint32_t seq_a, bool hb, XRecord pre, int site, float& ta, float& tb) {
+// With pl.xbcast, warp 0 alone polls and posts both totals as cluster_recv does.
+__device__ __forceinline__ void cluster_recv2(const StreamPlan& pl, const SmemLayout& L, const XCtx& xc, int warp,
+                                              int lane, uint32_t seq_a, bool hb, XRecord pre, int site, float& ta,
+                                              float& tb) {
   if (pl.xmode == kXGlobal) {
+    const uint32_t slot_a = seq_a & (kXSlots - 1);
+    const uint32_t slot_b = (seq_a + 1) & (kXSlots - 1);
+    if (pl.xbcast && warp != 0) {
+      mbar_wait(&L.xbar[slot_a], (seq_a / kXSlots) & 1u, site);
+      ta = L.xpart[slot_a * kMaxCluster];
+      tb = 0.f;
+      if (hb) {
+        mbar_wait(&L.xbar[slot_b], ((seq_a + 1) / kXSlots) & 1u, site);
+        tb = L.xpart[slot_b * kMaxCluster];
+      }
+      return;
+    }
     const bool mine = (lane & 15) < pl.P && (lane < 16 || hb);
     const uint32_t want = xrec_tag(pl, seq_a + static_cast<uint32_t>(lane >> 4));
     XRecord w = pre;
@@ -341,6 +355,14 @@ __device__ __forceinline__ void cluster_recv2(const StreamPlan& pl, const SmemLa
     for (int off = 8; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
     ta = __shfl_sync(0xffffffffu, v, 0);
     tb = __shfl_sync(0xffffffffu, v, 16);
+    if (pl.xbcast && lane == 0) {
+      L.xpart[slot_a * kMaxCluster] = ta;
+      mbar_arrive(&L.xbar[slot_a]);
+      if (hb) {
+        L.xpart[slot_b * kMaxCluster] = tb;
+        mbar_arrive(&L.xbar[slot_b]);
+      }
+    }
     return;
   }
   ta = cluster_recv<false>(pl, L, xc, 0, lane, seq_a, 0ull, site);  // cluster exchange
@@ -1097,7 +1119,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
     const int64_t npairs = (n_local + 1) >> 1;
     for (int64_t j = 0; j <= npairs; ++j) {
       const int64_t ra2 = 2 * (j - 1);  // pair j-1's first row
-      const XRecord pre = j >= 1 ? xrec_load2(pl, xc, lane, static_cast<uint32_t>(ra2)) : 0ull;
+      const XRecord pre =
+          j >= 1 && (!pl.xbcast || warp == 0) ? xrec_load2(pl, xc, lane, static_cast<uint32_t>(ra2)) : 0ull;
       if (j < npairs) {
         const int64_t ra = 2 * j;
         const bool hb = ra + 1 < n_local;
@@ -1126,7 +1149,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) fwd_stream_kernel(const Fw
       if (j >= 1) {
         const bool hb = ra2 + 1 < n_local;
         float tot[2];
-        cluster_recv2(pl, L, xc, lane, static_cast<uint32_t>(ra2), hb, pre, kSiteFwdCluster, tot[0], tot[1]);
+        cluster_recv2(pl, L, xc, warp, lane, static_cast<uint32_t>(ra2), hb, pre, kSiteFwdCluster, tot[0], tot[1]);
         for (int h = 0; h < (hb ? 2 : 1); ++h) {
           const int64_t r2 = ra2 + h;
           const int64_t row = cid + r2 * ncl;

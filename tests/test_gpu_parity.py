@@ -569,12 +569,14 @@ def test_split_row_pipeline_variants(monkeypatch, k, lag, dtype):
 @pytest.mark.parametrize("xmode", ["0", "1"])
 @pytest.mark.parametrize("rows,n,dtype", [(1, 65536, BF16), (74, 65536, BF16), (111, 65536, BF16),
                                            (301, 65536, F16), (148, 32768, BF16), (222, 32768, F16),
-                                           (1001, 65536, F16)])
+                                           (1001, 65536, F16), (1, 262144, BF16), (2, 262144, BF16),
+                                           (37, 262144, BF16), (300, 131072, F16), (55, 131072, BF16)])
 def test_split_row_pairs_match_row_by_row(monkeypatch, xmode, rows, n, dtype):
-    """Residual-free forwards with rows split over 2 or 4 CTAs take their rows in pairs (one
-    CTA-wide sum, one exchange round and one record poll per two rows). With odd and even
-    row counts per CTA (1, 2, 3 and more), cluster and global exchange, out and rstd must
-    equal the row-by-row loop's bit for bit and match the oracle."""
+    """Residual-free forwards with rows split over 2 to 16 CTAs take their rows in pairs (one
+    CTA-wide sum, one exchange round and one record poll per two rows; with the global
+    exchange warp 0 alone polls). With odd and even row counts per CTA (1, 2, 3 and more),
+    cluster and global exchange, out and rstd must equal the row-by-row loop's bit for bit
+    and match the oracle."""
     monkeypatch.setenv("RMSNORM_B200_XMODE", xmode)
     x = _g((rows, n), dtype, 400 + rows)
     w = _g((n,), F32, 401, "weight")
